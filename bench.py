@@ -1,0 +1,664 @@
+"""Benchmark of the fused layer-op chain (small-vLLM's per-layer, token-row-parallel ops).
+
+One step is one pass of the chain over the workload's token rows:
+    embedding gather -> add + RMSNorm -> Qwen3 q/k RMSNorm + RoPE -> SiLU(gate) * up
+each op on its own seeded synthetic inputs of the Qwen3-0.6B shapes (hidden 1024, 16/8 heads of
+128, intermediate 3072, vocab 151936). The default workload is the 1,048,576-token bandwidth
+sweep, token rows split evenly over the GPUs (strong scaling, no collective on the timed path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
+
+Prints ONE JSON line on rank 0. `value` is the whole-job algorithmic HBM GB/s of the chain
+(bytes every op must read and write, summed over ranks, over the slowest rank's device time);
+`e2e` is the same metric through svllm_ops with pinned host buffers, copies in the timed region.
+`--impl reference` times the reference's CPU path on this host's cores instead (the reference's
+own OpenMP rms_norm built from its sources, and the C/OpenMP restatement for the ops it lacks).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT / "small-vllm_b200" / "python"), str(ROOT / "oracle")]
+
+METRIC = "fused layer-op achieved HBM GB/s (% of B200 peak) and tokens/s at 1/2/4/8 GPUs"
+UNIT = "GB/s"
+
+QWEN3 = dict(hidden=1024, heads=16, kv_heads=8, head_dim=128, inter=3072, vocab=151936,
+             eps=1e-6, theta=1e6)
+
+# Algorithmic bytes per token of each op (bf16 activations; int32 ids; int64 positions):
+#   embedding     read the table row and write the output row, plus the id
+#   add_rms_norm  read x and residual, write residual' and the normed x
+#   qk_norm_rope  read and write q (16 x 128) and k (8 x 128) in place, plus the position
+#   silu_and_mul  read gate and up, write out
+def op_bytes(cfg: dict) -> dict[str, int]:
+    h, hd, inter = cfg["hidden"], cfg["head_dim"], cfg["inter"]
+    heads = cfg["heads"] + cfg["kv_heads"]
+    return {
+        "embedding": 2 * h * 2 + 4,
+        "add_rms_norm": 4 * h * 2,
+        "qk_norm_rope": 2 * heads * hd * 2 + 8,
+        "silu_and_mul": 3 * inter * 2,
+    }
+
+
+OPS = ["embedding", "add_rms_norm", "qk_norm_rope", "silu_and_mul"]
+WORKLOADS = {
+    # name: (total tokens, position range)
+    "sweep": (1_048_576, 32768),
+    "prefill": (70_000, 2048),
+    "decode": (256, 4096),
+}
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="sweep")
+    p.add_argument("--tokens", type=int, default=0, help="override total tokens")
+    p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-validate", action="store_true")
+    p.add_argument("--cpu-sample-tokens", type=int, default=32768)
+    return p.parse_args()
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text())
+    return {"hbm_gbs": 6650.0, "fallback": True}
+
+
+def split_rows(total: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous, balanced row range [begin, end) of `rank`."""
+    base, rem = divmod(total, world)
+    begin = rank * base + min(rank, rem)
+    return begin, begin + base + (1 if rank < rem else 0)
+
+
+# ---------------------------------------------------------------------------------------------
+# Synthetic inputs (seeded, per rank)
+
+def make_inputs(T: int, pos_hi: int, cfg: dict, device, seed: int):
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def randn(*shape, scale=1.0, shift=0.0):
+        t = torch.empty(shape, device=device, dtype=torch.bfloat16)
+        return t.normal_(shift, scale, generator=g) if shape[0] else t
+
+    h, hd = cfg["hidden"], cfg["head_dim"]
+    return {
+        "table": randn(cfg["vocab"], h, scale=0.02),
+        "ids": torch.randint(0, cfg["vocab"], (T,), device=device, dtype=torch.int32, generator=g),
+        "x": randn(T, h),
+        "residual": randn(T, h),
+        "w": randn(h, scale=0.1, shift=1.0),
+        "q": randn(T, cfg["heads"], hd),
+        "k": randn(T, cfg["kv_heads"], hd),
+        "qw": randn(hd, scale=0.1, shift=1.0),
+        "kw": randn(hd, scale=0.1, shift=1.0),
+        "pos": torch.randint(0, pos_hi, (T,), device=device, dtype=torch.int64, generator=g),
+        "gate": randn(T, cfg["inter"]),
+        "up": randn(T, cfg["inter"]),
+    }
+
+
+class Chain:
+    """The four ops through svllm_ops (LibTorch op layer -> C ABI -> sm_100a kernels)."""
+
+    def __init__(self, inp: dict, cfg: dict):
+        import torch
+        import svllm_ops
+
+        self.ops = svllm_ops
+        self.inp = inp
+        self.cfg = cfg
+        T = inp["ids"].shape[0]
+        self.emb_out = torch.empty(T, cfg["hidden"], device=inp["ids"].device, dtype=torch.bfloat16)
+        self.silu_out = torch.empty(T, cfg["inter"], device=inp["ids"].device, dtype=torch.bfloat16)
+
+    def run_op(self, name: str) -> None:
+        i, c, o = self.inp, self.cfg, self.ops
+        if name == "embedding":
+            self.emb_out = o.embedding(i["ids"], i["table"])
+        elif name == "add_rms_norm":
+            o.add_rms_norm(i["x"], i["residual"], i["w"], c["eps"])
+        elif name == "qk_norm_rope":
+            o.qk_norm_rope(i["q"], i["k"], i["qw"], i["kw"], i["pos"], c["eps"], c["theta"])
+        else:
+            self.silu_out = o.silu_and_mul(i["gate"], i["up"])
+
+
+# ---------------------------------------------------------------------------------------------
+# Clocks sampled during the timed region
+
+class ClockSampler:
+    """Samples SM clocks and clock-event reasons of the given GPUs during the timed region, from
+    a thread polling NVML every few milliseconds (the timed region can be shorter than
+    nvidia-smi's sampling interval). Reads settings only; changes nothing."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, gpus: list[int], enabled: bool = True, period_s: float = 0.005):
+        self.gpus = gpus
+        self.enabled = enabled
+        self.period = period_s
+        self.samples: list[tuple[int, float, float, int]] = []
+        self._stop = None
+        self._thread = None
+
+    def _poll(self):
+        import pynvml
+
+        handles = [pynvml.nvmlDeviceGetHandleByIndex(i) for i in self.gpus]
+        reasons_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or getattr(
+            pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        while not self._stop.is_set():
+            for i, h in zip(self.gpus, handles):
+                try:
+                    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    rs = reasons_fn(h)
+                    self.samples.append((i, float(sm), float(mx), int(rs)))
+                except pynvml.NVMLError:
+                    pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if not self.enabled:
+            return self
+        import threading
+
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+        except Exception:  # NVML missing: report no samples rather than fail the bench
+            return self
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._poll, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        reasons = set()
+        for _, _, _, bits in self.samples:
+            for bit, name in self.REASONS.items():
+                if bits & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(s[1] for s in self.samples),
+                "sm_max_mhz": max(s[2] for s in self.samples), "reasons": sorted(reasons),
+                "samples": len(self.samples), "source": "NVML, polled every 5 ms"}
+
+
+# ---------------------------------------------------------------------------------------------
+# The CPU path (the reference arm and the cpu_baseline): the reference's own OpenMP rms_norm
+# (built from its sources into oracle/_ref) where the reference has the op, and the C/OpenMP
+# restatement (oracle/) for the rest. Host-resident, all host threads.
+
+def cpu_chain_sample(tokens: int, cfg: dict, pos_hi: int, steps: int, min_seconds: float = 0.0):
+    import numpy as np
+    import torch
+
+    import oracle
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    ref = oracle.reference_module()
+    rng = np.random.default_rng(1234)
+    h, hd, inter = cfg["hidden"], cfg["head_dim"], cfg["inter"]
+
+    def bf16(*shape, scale=1.0, shift=0.0):
+        return oracle.f32_to_bf16((rng.standard_normal(shape, dtype=np.float32) * scale + shift))
+
+    table = bf16(cfg["vocab"], h, scale=0.02)
+    ids = rng.integers(0, cfg["vocab"], tokens, dtype=np.int32)
+    x, r, w = bf16(tokens, h), bf16(tokens, h), bf16(h, scale=0.1, shift=1.0)
+    q, k = bf16(tokens, cfg["heads"], hd), bf16(tokens, cfg["kv_heads"], hd)
+    qw, kw = bf16(hd, scale=0.1, shift=1.0), bf16(hd, scale=0.1, shift=1.0)
+    pos = rng.integers(0, pos_hi, tokens, dtype=np.int64)
+    gate, up = bf16(tokens, inter), bf16(tokens, inter)
+    inv = oracle.inv_freq(cfg["theta"], hd)
+
+    def as_t(a):
+        return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16)
+
+    tx, tr, tw, tq, tk = as_t(x), as_t(r), as_t(w), as_t(q), as_t(k)
+    tqw, tkw = as_t(qw), as_t(kw)
+    per_op = {op: 0.0 for op in OPS}
+    done = 0
+    t_start = time.perf_counter()
+    while done < steps or time.perf_counter() - t_start < min_seconds:
+        t0 = time.perf_counter()
+        oracle.embedding(ids, table)
+        t1 = time.perf_counter()
+        if ref is not None:
+            s = tx + tr  # LibTorch add, then the reference's rms_norm
+            ref.rms_norm(s, tw, cfg["eps"])
+        else:
+            oracle.add_rms_norm(x, r, w, cfg["eps"], inplace=True)
+        t2 = time.perf_counter()
+        if ref is not None:
+            qn = ref.rms_norm(tq.view(-1, hd), tqw, cfg["eps"])
+            kn = ref.rms_norm(tk.view(-1, hd), tkw, cfg["eps"])
+            oracle.rope(qn.view(torch.int16).numpy().view(np.uint16).reshape(q.shape),
+                        kn.view(torch.int16).numpy().view(np.uint16).reshape(k.shape), pos, inv,
+                        inplace=True)
+        else:
+            oracle.qk_norm_rope(q, k, qw, kw, pos, cfg["eps"], inv, inplace=True)
+        t3 = time.perf_counter()
+        oracle.silu_and_mul(gate, up)
+        t4 = time.perf_counter()
+        for op, dt in zip(OPS, (t1 - t0, t2 - t1, t3 - t2, t4 - t3)):
+            per_op[op] += dt
+        done += 1
+    nbytes = op_bytes(cfg)
+    total_s = sum(per_op.values())
+    gbs = sum(nbytes.values()) * tokens * done / total_s / 1e9
+    kind = "reference" if ref is not None else "port"
+    sample = (f"{tokens} tokens x {done} passes of the chain on host memory; "
+              + ("reference's own OpenMP rms_norm (oracle/_ref, built from its sources) for the "
+                 "norms, after a LibTorch add; C/OpenMP restatement (oracle/) for embedding, "
+                 "rope, silu_and_mul" if ref is not None else "C/OpenMP restatement (oracle/)"))
+    ops = {op: round(nbytes[op] * tokens * done / per_op[op] / 1e9, 2) for op in OPS}
+    return {"value": round(gbs, 2), "unit": UNIT, "cores": cores, "kind": kind, "sample": sample,
+            "ops_gbs": ops, "tokens_per_s": round(tokens * done / total_s, 1),
+            "ms_per_step": round(1e3 * total_s / done, 3)}
+
+
+# ---------------------------------------------------------------------------------------------
+
+def dist_setup(args):
+    """One process per GPU; NCCL for the barrier, the max-over-ranks timing and validation.
+    The reference arm runs on rank 0 alone and needs no process group."""
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def run_reference(args, world, rank) -> int:
+    cfg = QWEN3
+    total, pos_hi = WORKLOADS[args.workload]
+    total = args.tokens or total
+    if rank != 0:
+        return 0
+    tokens = min(args.cpu_sample_tokens, total)
+    # untimed warm-up passes, then exactly `steps` timed passes
+    cpu_chain_sample(min(tokens, 4096), cfg, pos_hi, max(1, args.warmup))
+    base = cpu_chain_sample(tokens, cfg, pos_hi, args.steps)
+    line = {
+        "metric": METRIC, "value": base["value"], "unit": UNIT, "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": base["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"qwen3-0.6b layer-op chain, {args.workload}", "tokens": total,
+                   "sample_tokens": tokens, "ops": OPS},
+        "tokens_per_s": base["tokens_per_s"], "ops_gbs": base["ops_gbs"],
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    args = parse_args()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+
+    import torch
+    import torch.distributed as dist
+
+    import svllm_ops
+
+    assert torch.cuda.is_available(), "bench.py (impl ours) needs a GPU"
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = QWEN3
+    total, pos_hi = WORKLOADS[args.workload]
+    total = args.tokens or total
+    begin, end = split_rows(total, world, rank)
+    T = end - begin
+    nbytes = op_bytes(cfg)
+    chain_bytes_per_token = sum(nbytes.values())
+
+    inp = make_inputs(T, pos_hi, cfg, dev, seed=1000 + rank)
+    chain = Chain(inp, cfg)
+    torch.cuda.synchronize()
+
+    validation = None
+    if not args.no_validate:
+        validation = validate(chain, inp, cfg, world, rank, dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        for op in OPS:
+            chain.run_op(op)
+    torch.cuda.synchronize()
+    assert svllm_ops.read_device_error(local, True) == 0
+
+    ev = {op: [] for op in OPS}
+    sampler = ClockSampler(list(range(world)) if world > 1 else [local], enabled=rank == 0)
+    barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        start = torch.cuda.Event(enable_timing=True)
+        stop = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            for op in OPS:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                chain.run_op(op)
+                e1.record(stream)
+                ev[op].append((e0, e1))
+        stop.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = start.elapsed_time(stop)
+    op_ms = {op: sum(a.elapsed_time(b) for a, b in ev[op]) / args.steps for op in OPS}
+
+    t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_ms = float(t.item()) / args.steps  # per step, slowest rank
+
+    # end to end through svllm_ops with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = measure_e2e(chain, inp, cfg, args, world, dev)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_chain_sample(min(args.cpu_sample_tokens, total), cfg, pos_hi, 2,
+                               min_seconds=5.0)
+
+    if rank == 0:
+        peaks = measured_peaks()
+        peak = float(peaks["hbm_gbs"])
+        value = chain_bytes_per_token * total / (max_ms * 1e-3) / 1e9
+        ops_gbs = {op: round(nbytes[op] * T / (op_ms[op] * 1e-3) / 1e9, 1) for op in OPS}
+        dominant = max(OPS, key=lambda op: op_ms[op])
+        traffic = load_traffic(dominant, T)
+        achieved = nbytes[dominant] * T / (op_ms[dominant] * 1e-3) / 1e9
+        clocks = sampler.summary()
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(max_ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"qwen3-0.6b layer-op chain, {args.workload}",
+                       "tokens": total, "tokens_per_gpu": T, "hidden": cfg["hidden"],
+                       "heads": [cfg["heads"], cfg["kv_heads"]], "head_dim": cfg["head_dim"],
+                       "intermediate": cfg["inter"], "vocab": cfg["vocab"],
+                       "positions": f"uniform [0, {pos_hi})", "ops": OPS,
+                       "l2": "no flush: every op's inputs exceed the 126 MB L2"
+                       if T * 2 * cfg["hidden"] > 126e6 else "inputs L2-resident (small T)",
+                       "parallelism": f"rows sharded over {world} GPU(s), no collective"},
+            "tokens_per_s": round(total / (max_ms * 1e-3), 1),
+            "frac_of_peak": round(value / (peak * world), 4),
+            "ops_gbs_per_gpu": ops_gbs,
+            "ops_ms_per_gpu": {op: round(op_ms[op], 4) for op in OPS},
+            "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic,
+                         "algorithmic_bytes": nbytes[dominant] * T,
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"
+                         if not peaks.get("fallback") else "fallback 6650 GB/s"},
+            "clocks": clocks,
+            "gpu_launches": len(OPS) * args.steps,
+            "e2e": e2e,
+            "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            if cpu else None,
+            "validation": validation,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def load_traffic(kernel_op: str, tokens: int):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, scaled to
+    this launch's tokens (traffic grows with the rows processed); None if there is none."""
+    path = ROOT / "profiles" / "dram_traffic.json"
+    if not path.exists():
+        return None
+    data = json.loads(path.read_text())
+    entry = data.get(kernel_op)
+    if not entry:
+        return None
+    return round(entry["bytes_per_token"] * tokens)
+
+
+# ---------------------------------------------------------------------------------------------
+# Validation (outside every timed region): a sample of each rank's rows is checked against the
+# oracle after an NCCL all-gather of the output shards to rank 0.
+
+def validate(chain, inp, cfg, world, rank, dev, rows: int = 256):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import oracle
+
+    n = min(rows, inp["ids"].shape[0])
+
+    def bits(t):
+        return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+    saved = {k: inp[k][:n].clone() for k in ("ids", "x", "residual", "q", "k", "pos", "gate",
+                                            "up")}
+    for op in OPS:
+        chain.run_op(op)
+    torch.cuda.synchronize()
+    outs = [chain.emb_out[:n], inp["x"][:n], inp["residual"][:n], inp["q"][:n].reshape(n, -1),
+            inp["k"][:n].reshape(n, -1), chain.silu_out[:n]]
+    packed = torch.cat([o.reshape(n, -1) for o in outs], dim=1).contiguous()
+    ins = torch.cat([saved[k].reshape(n, -1).view(torch.int16)
+                     for k in ("x", "residual", "q", "k", "gate", "up")], dim=1).contiguous()
+    ids_pos = torch.stack([saved["ids"].to(torch.int64), saved["pos"]], dim=1).contiguous()
+    if world > 1:
+        g_out = [torch.empty_like(packed) for _ in range(world)]
+        g_in = [torch.empty_like(ins) for _ in range(world)]
+        g_ip = [torch.empty_like(ids_pos) for _ in range(world)]
+        dist.all_gather(g_out, packed)
+        dist.all_gather(g_in, ins)
+        dist.all_gather(g_ip, ids_pos)
+    else:
+        g_out, g_in, g_ip = [packed], [ins], [ids_pos]
+    if rank != 0:
+        return None
+    h, hd, inter = cfg["hidden"], cfg["head_dim"], cfg["inter"]
+    nq, nk = cfg["heads"] * hd, cfg["kv_heads"] * hd
+    table = bits(inp["table"])
+    inv = svllm_inv(cfg)
+    worst = 0
+    mismatched = 0
+    for r in range(world):
+        o = bits(g_out[r].view(torch.bfloat16))
+        i = g_in[r].cpu().numpy().view(np.uint16)
+        ip = g_ip[r].cpu().numpy()
+        x, res = i[:, :h], i[:, h:2 * h]
+        q, k = i[:, 2 * h:2 * h + nq], i[:, 2 * h + nq:2 * h + nq + nk]
+        gate = i[:, 2 * h + nq + nk:2 * h + nq + nk + inter]
+        up = i[:, 2 * h + nq + nk + inter:]
+        emb, bad = oracle.embedding(ip[:, 0].astype(np.int32), table)
+        ox, orr = oracle.add_rms_norm(x, res, bits(inp["w"]), cfg["eps"])
+        oq, ok = oracle.qk_norm_rope(q.reshape(n, -1, hd), k.reshape(n, -1, hd), bits(inp["qw"]),
+                                     bits(inp["kw"]), ip[:, 1], cfg["eps"], inv)
+        oy = oracle.silu_and_mul(gate, up)
+        col = 0
+        for name, ref, width in (("embedding", emb, h), ("x", ox, h), ("residual", orr, h),
+                                 ("q", oq.reshape(n, -1), nq), ("k", ok.reshape(n, -1), nk),
+                                 ("silu", oy, inter)):
+            got = o[:, col:col + width]
+            col += width
+            d = np.abs(key(got) - key(ref))
+            worst = max(worst, int(d.max()))
+            mismatched += int((d > 0).sum())
+        if bad:
+            worst = max(worst, 1 << 20)
+    return {"rows_per_gpu": n, "gathered_from": world, "worst_bf16_ulp": worst,
+            "elements_not_bit_exact": mismatched,
+            "ok": worst <= 2}
+
+
+def key(bits_arr):
+    import numpy as np
+
+    b = bits_arr.astype(np.int32)
+    return np.where(b & 0x8000, -(b & 0x7FFF), b)
+
+
+def svllm_inv(cfg):
+    import svllm_ops
+
+    return svllm_ops.rope_inv_freq(cfg["theta"], cfg["head_dim"]).numpy()
+
+
+# ---------------------------------------------------------------------------------------------
+# End to end: pinned host inputs -> device -> chain through svllm_ops -> pinned host outputs,
+# pipelined in chunks over three streams (copy in, compute, copy out) so PCIe runs both ways
+# while the kernels work. Every step copies all of that step's inputs in and outputs out.
+
+def measure_e2e(chain, inp, cfg, args, world, dev):
+    import torch
+    import torch.distributed as dist
+
+    import svllm_ops
+
+    T = inp["ids"].shape[0]
+    names_in = ["ids", "x", "residual", "q", "k", "pos", "gate", "up"]
+    host_in = {k: torch.empty(inp[k].shape, dtype=inp[k].dtype, pin_memory=True)
+               for k in names_in}
+    for k in names_in:
+        host_in[k].copy_(inp[k])
+    out_shapes = {"emb": (T, cfg["hidden"]), "x": (T, cfg["hidden"]),
+                  "residual": (T, cfg["hidden"]), "q": tuple(inp["q"].shape),
+                  "k": tuple(inp["k"].shape), "silu": (T, cfg["inter"])}
+    host_out = {k: torch.empty(s, dtype=torch.bfloat16, pin_memory=True)
+                for k, s in out_shapes.items()}
+    silu_dev = torch.empty(T, cfg["inter"], device=dev, dtype=torch.bfloat16)
+    emb_dev = torch.empty(T, cfg["hidden"], device=dev, dtype=torch.bfloat16)
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    d2h = sum(t.numel() * t.element_size() for t in host_out.values())
+
+    chunks = max(1, min(16, T // 16384))
+    bounds = [(T * c // chunks, T * (c + 1) // chunks) for c in range(chunks)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    s_comp = torch.cuda.current_stream(dev)
+
+    done_out: list = [None] * len(bounds)
+
+    def step():
+        done_in, done_comp = [], []
+        for c, (a, b) in enumerate(bounds):
+            with torch.cuda.stream(s_in):
+                if done_out[c] is not None:
+                    # the previous step's copy-out of this chunk must finish before we overwrite
+                    s_in.wait_event(done_out[c])
+                for k in names_in:
+                    inp[k][a:b].copy_(host_in[k][a:b], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(s_in)
+                done_in.append(e)
+        for c, (a, b) in enumerate(bounds):
+            s_comp.wait_event(done_in[c])
+            emb = svllm_ops.embedding(inp["ids"][a:b], inp["table"])
+            emb_dev[a:b].copy_(emb, non_blocking=True)
+            svllm_ops.add_rms_norm(inp["x"][a:b], inp["residual"][a:b], inp["w"], cfg["eps"])
+            svllm_ops.qk_norm_rope(inp["q"][a:b], inp["k"][a:b], inp["qw"], inp["kw"],
+                                   inp["pos"][a:b], cfg["eps"], cfg["theta"])
+            silu_dev[a:b].copy_(svllm_ops.silu_and_mul(inp["gate"][a:b], inp["up"][a:b]),
+                                non_blocking=True)
+            e = torch.cuda.Event()
+            e.record(s_comp)
+            done_comp.append(e)
+        for c, (a, b) in enumerate(bounds):
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done_comp[c])
+                host_out["emb"][a:b].copy_(emb_dev[a:b], non_blocking=True)
+                host_out["x"][a:b].copy_(inp["x"][a:b], non_blocking=True)
+                host_out["residual"][a:b].copy_(inp["residual"][a:b], non_blocking=True)
+                host_out["q"][a:b].copy_(inp["q"][a:b], non_blocking=True)
+                host_out["k"][a:b].copy_(inp["k"][a:b], non_blocking=True)
+                host_out["silu"][a:b].copy_(silu_dev[a:b], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(s_out)
+                done_out[c] = e
+
+    step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record(s_comp)
+    for _ in range(args.steps):
+        step()
+    s_comp.wait_stream(s_out)
+    s_comp.wait_stream(s_in)
+    stop.record(s_comp)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / args.steps
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    total = T * world if world > 1 else T
+    if world > 1:
+        tt = torch.tensor([T], device=dev, dtype=torch.int64)
+        dist.all_reduce(tt)
+        total = int(tt.item())
+    value = sum(op_bytes(cfg).values()) * total / (ms * 1e-3) / 1e9
+    return {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d * world,
+            "d2h_bytes_per_step": d2h * world, "ms_per_step": round(ms, 3),
+            "chunks": chunks, "api": "svllm_ops (pinned host buffers, 3 streams)"}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,204 @@
+/*
+ * svllm_kernels.h - C ABI of the sm_100a layer-op kernels (libsvllm_kernels.so).
+ *
+ * These are the memory-bound, token-row-parallel ops around every GEMM of a Qwen3 / Llama
+ * decoder layer: RMSNorm, RMSNorm with the fused residual add, Qwen3's per-head q/k RMSNorm
+ * fused with rotary embedding, rotary embedding alone (plain theta or Llama-3 frequency
+ * scaling), SiLU(gate) * up, and the token-embedding gather.
+ *
+ * Conventions (every entry point):
+ *   - Plain pointers and sizes only. Tensor pointers are DEVICE pointers on the current CUDA
+ *     device; `stream` is a cudaStream_t (NULL = the legacy default stream). Work is enqueued
+ *     on `stream` and the call returns without synchronising: no host sync, no allocation, so
+ *     every entry point may be captured in a CUDA graph.
+ *   - Rows are `num_rows` (or `num_tokens`) rows of `hidden` elements; a row stride is given in
+ *     elements and must be >= the row length. The last dimension is always contiguous.
+ *   - bf16 is IEEE bfloat16 (2 bytes); the *_f32 variants take fp32. Arithmetic is fp32.
+ *   - The return value is an svllm_status; svllm_status_string() names it. A call that returns
+ *     an error has enqueued nothing. No entry point throws.
+ *   - 16-byte aligned pointers and strides with a row length that is a multiple of 16 bytes take
+ *     the bulk-copy (TMA) path; anything else takes a plain-load path on the GPU. There is no
+ *     CPU path behind these functions.
+ *   - `err` (optional, may be NULL) is a device int the kernel ORs SVLLM_DEVERR_* bits into.
+ *     With NULL the library's own per-device word is used; svllm_read_device_error reads it.
+ *
+ * Reference interfaces these replace or extend (small-vLLM, paths within its project):
+ *   src/ops/rms_norm.h:13            at::Tensor svllm::ops::rms_norm(x, weight, eps)
+ *   src/ops/rms_norm_kernels.h:38-40 svllm::ops::cuda_impl::rms_norm(out, x, weight, eps)
+ *   src/ops/cuda/rms_norm.cu:103-131 the CUDA launcher this library's calls stand in for
+ *   bindings/svllm_ops.cpp:18        the Python binding the op layer above this ABI keeps
+ *   src/model/config.h:10-15         Llama3RopeScaling, mirrored by svllm_llama3_scaling
+ * The other five ops have no implementation in the reference; they are added in its op
+ * convention (one op per src/ops/<op>.{h,cpp}, docs/design-spec.md:28 "Fused CUDA kernels",
+ * docs/ROADMAP.md:40 "RoPE with QK-norm", "SiLU-and-mul").
+ */
+#ifndef SVLLM_KERNELS_H_
+#define SVLLM_KERNELS_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without including the CUDA headers. */
+struct CUstream_st;
+typedef struct CUstream_st* svllm_stream;
+
+typedef enum svllm_status {
+  SVLLM_OK = 0,
+  SVLLM_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad size, stride or dtype */
+  SVLLM_ERR_TOO_LARGE = 2,        /* sizes exceed the kernel's index range */
+  SVLLM_ERR_UNSUPPORTED = 3,      /* a shape this build has no kernel for */
+  SVLLM_ERR_LAUNCH = 4,           /* the kernel launch failed */
+  SVLLM_ERR_CUDA = 5              /* another CUDA runtime call failed */
+} svllm_status;
+
+/* Bits of the device error word. */
+#define SVLLM_DEVERR_BAD_INDEX 1    /* an embedding id outside [0, vocab): its row is zeroed */
+#define SVLLM_DEVERR_WAIT_TIMEOUT 2 /* a bulk copy did not land in time: the kernel stopped */
+
+/* Index dtype of positions / token ids. */
+typedef enum svllm_index_type { SVLLM_INDEX_I32 = 0, SVLLM_INDEX_I64 = 1 } svllm_index_type;
+
+/* Llama-3 RoPE frequency scaling (rope_type "llama3"); mirrors src/model/config.h:10-15. */
+typedef struct svllm_llama3_scaling {
+  double factor;
+  double low_freq_factor;
+  double high_freq_factor;
+  int64_t original_max_position_embeddings;
+} svllm_llama3_scaling;
+
+/* Returns a static, human-readable name for a status code. */
+const char* svllm_status_string(int status);
+
+/* Library version, "0.1.0" (the reference's pyproject.toml:3 version). */
+const char* svllm_version(void);
+
+/*
+ * RMSNorm.  out = round(round(x * rsqrt(mean(x^2) + eps)) * weight), fp32 sum of squares,
+ * round() being the output dtype's rounding (identity for fp32), i.e. the reference's
+ * src/ops/cuda/rms_norm.cu:62-95 and src/ops/cpu/rms_norm.cpp:13-44 formula.
+ * x, out: [num_rows, hidden] with row strides; weight: [hidden] contiguous.
+ * Replaces: svllm::ops::cuda_impl::rms_norm (src/ops/rms_norm_kernels.h:38-40).
+ */
+int svllm_rms_norm_bf16(void* out, const void* x, const void* weight, int64_t num_rows,
+                        int64_t hidden, int64_t out_row_stride, int64_t x_row_stride, float eps,
+                        svllm_stream stream);
+int svllm_rms_norm_f32(float* out, const float* x, const float* weight, int64_t num_rows,
+                       int64_t hidden, int64_t out_row_stride, int64_t x_row_stride, float eps,
+                       svllm_stream stream);
+
+/*
+ * RMSNorm with the fused residual add, in place (Hugging Face decoder-layer semantics):
+ *   residual <- round(x + residual);   x <- rms_norm(residual, weight, eps)
+ * x, residual: [num_rows, hidden] with row strides; weight: [hidden].
+ * New op in the reference's convention (planned at docs/design-spec.md:28).
+ */
+int svllm_add_rms_norm_bf16(void* x, void* residual, const void* weight, int64_t num_rows,
+                            int64_t hidden, int64_t x_row_stride, int64_t residual_row_stride,
+                            float eps, svllm_stream stream);
+int svllm_add_rms_norm_f32(float* x, float* residual, const float* weight, int64_t num_rows,
+                           int64_t hidden, int64_t x_row_stride, int64_t residual_row_stride,
+                           float eps, svllm_stream stream);
+
+/*
+ * Qwen3 per-head q/k RMSNorm fused with neox-style rotary embedding, in place.
+ *   q: [num_tokens, num_heads, head_dim] (token row stride q_row_stride, heads contiguous)
+ *   k: [num_tokens, num_kv_heads, head_dim] (token row stride k_row_stride)
+ *   q_weight, k_weight: [head_dim]; positions: [num_tokens] of pos_type.
+ *   inv_freq: HOST array of head_dim/2 fp32 inverse frequencies (see svllm_rope_inv_freq); it
+ *   is passed to the kernel by value, so the caller may free it when the call returns.
+ * Per head: h = round(round(x * rsqrt(mean(x^2) + eps)) * w); then for i < head_dim/2, with
+ * a = fp32(pos) * inv_freq[i], c = round(cos a), s = round(sin a):
+ *   out[i] = round(round(h[i] * c) - round(h[i + d/2] * s))
+ *   out[i + d/2] = round(round(h[i + d/2] * c) + round(h[i] * s))
+ * which is Qwen3RMSNorm followed by apply_rotary_pos_emb with bf16 cos/sin. head_dim must be
+ * even and at most 512. Flags: src/model/config.h:29 (qk_norm), config.h:27 (rope_theta).
+ */
+int svllm_qk_norm_rope_bf16(void* q, void* k, const void* q_weight, const void* k_weight,
+                            const void* positions, int pos_type, int64_t num_tokens,
+                            int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                            int64_t q_row_stride, int64_t k_row_stride, float eps,
+                            const float* inv_freq, svllm_stream stream);
+int svllm_qk_norm_rope_f32(float* q, float* k, const float* q_weight, const float* k_weight,
+                           const void* positions, int pos_type, int64_t num_tokens,
+                           int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                           int64_t q_row_stride, int64_t k_row_stride, float eps,
+                           const float* inv_freq, svllm_stream stream);
+
+/*
+ * Neox-style rotary embedding alone, in place on q and k (Llama: no q/k norm). Same layout,
+ * formula and inv_freq convention as svllm_qk_norm_rope_* without the norm.
+ * Llama-3 scaling enters only through inv_freq (svllm_rope_inv_freq with a scaling struct).
+ */
+int svllm_rope_bf16(void* q, void* k, const void* positions, int pos_type, int64_t num_tokens,
+                    int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                    int64_t q_row_stride, int64_t k_row_stride, const float* inv_freq,
+                    svllm_stream stream);
+int svllm_rope_f32(float* q, float* k, const void* positions, int pos_type, int64_t num_tokens,
+                   int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                   int64_t q_row_stride, int64_t k_row_stride, const float* inv_freq,
+                   svllm_stream stream);
+
+/*
+ * Host helper: the rotary inverse-frequency table, head_dim/2 fp32 values written to the HOST
+ * array inv_freq, by Hugging Face's fp32 formula: inv[i] = 1 / powf(theta, fp32(2i) / head_dim)
+ * with every step an fp32 operation. With scaling != NULL the Llama-3 rule
+ * (src/model/config.h:10-15) follows, also in fp32: wavelength w = 2*pi / inv;
+ * w > orig/low_freq_factor -> inv/factor; w < orig/high_freq_factor -> inv; otherwise
+ * (1 - s) * inv / factor + s * inv with s = (orig / w - low) / (high - low).
+ * torch's fp32 pow and the C library's powf agree on almost every entry; the LibTorch op layer
+ * builds the table with torch itself, so that it equals Hugging Face's bit for bit.
+ */
+int svllm_rope_inv_freq(double theta, int64_t head_dim, const svllm_llama3_scaling* scaling,
+                        float* inv_freq);
+
+/*
+ * SiLU(gate) * up.  out = round(round(gate / (1 + exp(-gate))) * up).
+ * gate, up, out: [num_rows, inter] with row strides (gate and up may be the two halves of one
+ * [num_rows, 2 * inter] tensor). New op (docs/ROADMAP.md:40 "SiLU-and-mul").
+ */
+int svllm_silu_and_mul_bf16(void* out, const void* gate, const void* up, int64_t num_rows,
+                            int64_t inter, int64_t out_row_stride, int64_t gate_row_stride,
+                            int64_t up_row_stride, svllm_stream stream);
+int svllm_silu_and_mul_f32(float* out, const float* gate, const float* up, int64_t num_rows,
+                           int64_t inter, int64_t out_row_stride, int64_t gate_row_stride,
+                           int64_t up_row_stride, svllm_stream stream);
+
+/*
+ * Token-embedding gather, a bit-exact row copy: out[t] = table[ids[t]].
+ * ids: [num_tokens] of id_type; table: [vocab_size, hidden] (row stride table_row_stride);
+ * out: [num_tokens, hidden] (row stride out_row_stride). An id outside [0, vocab_size) zeroes
+ * its output row and raises SVLLM_DEVERR_BAD_INDEX in *err (or the library word); it never
+ * faults. The table is model.embed_tokens.weight (tests/cpp/safetensors_test.cpp:161-162);
+ * ids are int32 as the tokenizer returns them (src/tokenizer/tokenizer.h:22) or int64.
+ */
+int svllm_embedding_bf16(void* out, const void* ids, int id_type, const void* table,
+                         int64_t num_tokens, int64_t vocab_size, int64_t hidden,
+                         int64_t out_row_stride, int64_t table_row_stride, int* err,
+                         svllm_stream stream);
+int svllm_embedding_f32(float* out, const void* ids, int id_type, const float* table,
+                        int64_t num_tokens, int64_t vocab_size, int64_t hidden,
+                        int64_t out_row_stride, int64_t table_row_stride, int* err,
+                        svllm_stream stream);
+
+/*
+ * Reads (and with reset != 0 clears) the library's own error word on `device`. Synchronises
+ * that device. For validation, not for the hot path.
+ */
+int svllm_read_device_error(int device, int reset, int* flags);
+
+/*
+ * Tuning knob for the bulk-copy pipelines of one op ("rms_norm", "add_rms_norm", "qk_norm_rope",
+ * "rope", "silu_and_mul", "embedding"): target bytes per pipeline stage, stages per warp and
+ * warps per CTA; 0 keeps the current value. Results do not depend on it. Not thread-safe
+ * against concurrent launches of the same op.
+ */
+int svllm_set_pipeline(const char* op, int64_t unit_bytes, int64_t stages, int64_t warps);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SVLLM_KERNELS_H_ */

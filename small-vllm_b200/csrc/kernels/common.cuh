@@ -1,0 +1,246 @@
+// Device-side building blocks shared by the sm_100a layer-op kernels.
+//
+// Everything here is memory plumbing for token-row-parallel streaming ops: bf16 <-> fp32
+// conversion with the rounding the Hugging Face composites use, 16-byte vectors, mbarrier and
+// bulk-copy (TMA, non-tensor, never multicast) wrappers, bounded waits, and the device error
+// word that kernels raise instead of trapping.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace svllm::k {
+
+constexpr int kWarpSize = 32;
+
+// Device error word bits. A kernel never traps: it records the condition here and carries on
+// (bad ids) or stops its own work (a wait that ran out), so the CUDA context stays usable.
+constexpr int kErrBadIndex = 1;     // an embedding id outside [0, vocab)
+constexpr int kErrWaitTimeout = 2;  // a bulk copy did not land within the wait limit
+
+// A wait on an mbarrier gives up after this many nanoseconds of %globaltimer.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// ---------------------------------------------------------------------------------------------
+// Element types. The kernels are written once over Elem and instantiated for bf16 and fp32.
+
+struct Bf16 {
+  using Storage = __nv_bfloat16;
+  static constexpr int kPerVec = 8;  // elements per 16-byte vector
+  __device__ static __forceinline__ float to_float(Storage v) { return __bfloat162float(v); }
+  __device__ static __forceinline__ Storage from_float(float v) { return __float2bfloat16_rn(v); }
+  // Round an fp32 intermediate to the storage type and back, as a bf16 torch op does.
+  __device__ static __forceinline__ float round(float v) {
+    return __bfloat162float(__float2bfloat16_rn(v));
+  }
+};
+
+struct F32 {
+  using Storage = float;
+  static constexpr int kPerVec = 4;
+  __device__ static __forceinline__ float to_float(Storage v) { return v; }
+  __device__ static __forceinline__ Storage from_float(float v) { return v; }
+  __device__ static __forceinline__ float round(float v) { return v; }
+};
+
+// Unpack a 16-byte vector into kPerVec floats, and pack kPerVec floats (rounded) back.
+template <class E>
+__device__ __forceinline__ void unpack(const uint4& raw, float (&f)[E::kPerVec]);
+
+template <>
+__device__ __forceinline__ void unpack<Bf16>(const uint4& raw, float (&f)[8]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // bf16 -> fp32 is exact: the bf16 bits are the high half of the fp32 bits
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+template <>
+__device__ __forceinline__ void unpack<F32>(const uint4& raw, float (&f)[4]) {
+  f[0] = __uint_as_float(raw.x);
+  f[1] = __uint_as_float(raw.y);
+  f[2] = __uint_as_float(raw.z);
+  f[3] = __uint_as_float(raw.w);
+}
+
+template <class E>
+__device__ __forceinline__ uint4 pack(const float (&f)[E::kPerVec]);
+
+template <>
+__device__ __forceinline__ uint4 pack<Bf16>(const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // cvt.rn.bf16x2.f32 rounds both halves to nearest even, like __float2bfloat16_rn
+    const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <>
+__device__ __forceinline__ uint4 pack<F32>(const float (&f)[4]) {
+  return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                    __float_as_uint(f[3]));
+}
+
+// ---------------------------------------------------------------------------------------------
+// Global memory access with streaming hints.
+
+__device__ __forceinline__ uint4 ld_global_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void st_global_v4(void* p, const uint4& v) {
+  asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_shared_v4(const void* p) {
+  uint4 r;
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "r"(a));
+  return r;
+}
+
+// ---------------------------------------------------------------------------------------------
+// mbarrier + bulk copy (cp.async.bulk, the non-tensor TMA path). No .multicast::cluster form is
+// used anywhere in this library: every copy moves this GPU's own memory into its own CTA.
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+// Makes initialised mbarriers visible to the async proxy before the first bulk copy uses them.
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Orders this thread's earlier generic-proxy shared-memory accesses before later async-proxy
+// ones (a bulk copy overwriting a stage the warp has just read, or a bulk store of a stage the
+// warp has just written).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for the phase with the given parity to complete. Returns false if it has not after
+// kWaitLimitNs; the caller then raises kErrWaitTimeout and stops.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) {
+    return true;
+  }
+  const uint64_t start = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - start > kWaitLimitNs) {
+      return false;
+    }
+  }
+  return true;
+}
+
+// Global -> shared bulk copy completing on an mbarrier. dst, src and bytes are multiples of 16.
+__device__ __forceinline__ void bulk_load(void* dst_smem, const void* src_gmem, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// Shared -> global bulk store, tracked by this thread's bulk groups.
+__device__ __forceinline__ void bulk_store(void* dst_gmem, const void* src_smem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst_gmem),
+               "r"(smem_addr(src_smem)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Waits until at most N of this thread's bulk groups still have to read their shared source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Error word. The host passes either the caller's device int or the library's own per-device
+// word (read back with svllm_read_device_error), so err is never null in a kernel.
+
+__device__ __forceinline__ void raise_error(int* err, int bits) { atomicOr(err, bits); }
+
+// ---------------------------------------------------------------------------------------------
+// Reductions.
+
+// Sum over aligned groups of G lanes (G a power of two, at most 32) by xor butterflies: every
+// lane of a group ends with the same value.
+template <int G>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int offset = G / 2; offset > 0; offset /= 2) {
+    v += __shfl_xor_sync(0xffffffffu, v, offset);
+  }
+  return v;
+}
+
+// Balanced contiguous partition of n units over `parts` workers: worker i gets [begin, end).
+__device__ __forceinline__ void partition(int64_t n, int64_t parts, int64_t i, int64_t& begin,
+                                          int64_t& end) {
+  const int64_t base = n / parts;
+  const int64_t rem = n % parts;
+  begin = i * base + (i < rem ? i : rem);
+  end = begin + base + (i < rem ? 1 : 0);
+}
+
+}  // namespace svllm::k

@@ -1,0 +1,192 @@
+// Host-side launch plumbing and the small C-ABI entry points that launch no kernel.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstring>
+#include <mutex>
+
+#include "host_common.h"
+
+namespace svllm::k {
+
+// The library's own device error word; callers that pass no err pointer read it back with
+// svllm_read_device_error.
+__device__ int g_library_error_word = 0;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+std::atomic<int> g_sm_count[kMaxDevices];
+std::atomic<int*> g_error_word[kMaxDevices];
+
+PipelineShape g_shapes[static_cast<int>(OpId::kCount)] = {
+    {8192, 4, 4},   // rms_norm
+    {8192, 4, 4},   // add_rms_norm
+    {8192, 4, 4},   // qk_norm_rope (a unit is one token; unit_bytes is unused)
+    {8192, 4, 4},   // rope
+    {8192, 4, 4},   // silu_and_mul
+    {8192, 4, 4},   // embedding
+};
+
+const char* const kOpNames[] = {"rms_norm", "add_rms_norm", "qk_norm_rope",
+                                "rope",     "silu_and_mul", "embedding"};
+
+struct OccEntry {
+  const void* func;
+  int threads;
+  size_t smem;
+  int device;
+  int blocks;
+};
+
+std::mutex g_occ_mutex;
+constexpr int kOccCacheSize = 256;
+OccEntry g_occ[kOccCacheSize];
+int g_occ_used = 0;
+
+struct AttrEntry {
+  const void* func;
+  int device;
+};
+AttrEntry g_attr[kOccCacheSize];
+int g_attr_used = 0;
+
+}  // namespace
+
+PipelineShape pipeline_shape(OpId op) { return g_shapes[static_cast<int>(op)]; }
+
+int set_pipeline_shape(const char* op, int64_t unit_bytes, int64_t stages, int64_t warps) {
+  if (op == nullptr || unit_bytes < 0 || stages < 0 || warps < 0 || unit_bytes > (1 << 20) ||
+      stages > 16 || warps > 32 || (unit_bytes % 16) != 0) {
+    return SVLLM_ERR_INVALID_ARGUMENT;
+  }
+  for (int i = 0; i < static_cast<int>(OpId::kCount); ++i) {
+    if (std::strcmp(op, kOpNames[i]) == 0) {
+      if (unit_bytes) g_shapes[i].unit_bytes = static_cast<int>(unit_bytes);
+      if (stages) g_shapes[i].stages = static_cast<int>(stages);
+      if (warps) g_shapes[i].warps = static_cast<int>(warps);
+      return SVLLM_OK;
+    }
+  }
+  return SVLLM_ERR_INVALID_ARGUMENT;
+}
+
+int current_device(int* device) {
+  return cudaGetDevice(device) == cudaSuccess && *device >= 0 && *device < kMaxDevices
+             ? SVLLM_OK
+             : SVLLM_ERR_CUDA;
+}
+
+int sm_count(int device) {
+  int n = g_sm_count[device].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+        n <= 0) {
+      n = 1;
+    }
+    g_sm_count[device].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
+int blocks_per_sm(const void* func, int threads, size_t smem_bytes, int device) {
+  const std::lock_guard<std::mutex> lock(g_occ_mutex);
+  for (int i = 0; i < g_occ_used; ++i) {
+    const OccEntry& e = g_occ[i];
+    if (e.func == func && e.threads == threads && e.smem == smem_bytes && e.device == device) {
+      return e.blocks;
+    }
+  }
+  bool attr_set = false;
+  for (int i = 0; i < g_attr_used; ++i) {
+    if (g_attr[i].func == func && g_attr[i].device == device) {
+      attr_set = true;
+      break;
+    }
+  }
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kMaxSmemPerCta)) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    if (g_attr_used < kOccCacheSize) g_attr[g_attr_used++] = {func, device};
+  }
+  int blocks = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, func, threads, smem_bytes) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (g_occ_used < kOccCacheSize) g_occ[g_occ_used++] = {func, threads, smem_bytes, device, blocks};
+  return blocks;
+}
+
+int* library_error_word(int device) {
+  int* p = g_error_word[device].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_library_error_word) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    p = static_cast<int*>(addr);
+    g_error_word[device].store(p, std::memory_order_release);
+  }
+  return p;
+}
+
+}  // namespace svllm::k
+
+using namespace svllm::k;
+
+extern "C" {
+
+const char* svllm_status_string(int status) {
+  switch (status) {
+    case SVLLM_OK:
+      return "ok";
+    case SVLLM_ERR_INVALID_ARGUMENT:
+      return "invalid argument (null pointer, size, stride, alignment or dtype)";
+    case SVLLM_ERR_TOO_LARGE:
+      return "sizes exceed the kernel's index range";
+    case SVLLM_ERR_UNSUPPORTED:
+      return "no kernel for this shape";
+    case SVLLM_ERR_LAUNCH:
+      return "kernel launch failed";
+    case SVLLM_ERR_CUDA:
+      return "CUDA runtime call failed";
+    default:
+      return "unknown status";
+  }
+}
+
+const char* svllm_version(void) { return "0.1.0"; }
+
+int svllm_read_device_error(int device, int reset, int* flags) {
+  if (flags == nullptr || device < 0 || device >= kMaxDevices) {
+    return SVLLM_ERR_INVALID_ARGUMENT;
+  }
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess || cudaSetDevice(device) != cudaSuccess) {
+    return SVLLM_ERR_CUDA;
+  }
+  int status = SVLLM_OK;
+  int* word = library_error_word(device);
+  if (word == nullptr || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpy(flags, word, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+    status = SVLLM_ERR_CUDA;
+  } else if (reset && cudaMemset(word, 0, sizeof(int)) != cudaSuccess) {
+    status = SVLLM_ERR_CUDA;
+  }
+  if (status != SVLLM_OK) cudaGetLastError();
+  cudaSetDevice(prev);
+  return status;
+}
+
+int svllm_set_pipeline(const char* op, int64_t unit_bytes, int64_t stages, int64_t warps) {
+  return set_pipeline_shape(op, unit_bytes, stages, warps);
+}
+
+}  // extern "C"

@@ -1,0 +1,57 @@
+// Host-side launch plumbing shared by the C-ABI entry points: argument checks, device
+// properties and occupancy caches, the per-op pipeline shape, and the device error word.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "svllm_kernels.h"
+
+namespace svllm::k {
+
+// Shape of one op's bulk-copy pipeline: target bytes per stage, stages per warp, warps per CTA.
+struct PipelineShape {
+  int unit_bytes;
+  int stages;
+  int warps;
+};
+
+enum class OpId { kRmsNorm, kAddRmsNorm, kQkNormRope, kRope, kSiluAndMul, kEmbedding, kCount };
+
+PipelineShape pipeline_shape(OpId op);
+int set_pipeline_shape(const char* op, int64_t unit_bytes, int64_t stages, int64_t warps);
+
+// The current device and its SM count (cached per device).
+int current_device(int* device);
+int sm_count(int device);
+
+// Maximum resident CTAs of `func` per SM for this block size and dynamic shared memory. Raises
+// the function's dynamic shared-memory limit the first time it is seen on a device.
+int blocks_per_sm(const void* func, int threads, size_t smem_bytes, int device);
+
+// Largest dynamic shared memory a CTA may use on this architecture.
+constexpr size_t kMaxSmemPerCta = 227 * 1024;
+
+// The library's own error word on `device` (a __device__ int, address cached per device).
+int* library_error_word(int device);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+// Maps the launch's cudaGetLastError() to a status.
+inline int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? SVLLM_OK : SVLLM_ERR_LAUNCH;
+}
+
+// Grid size for a persistent kernel: enough CTAs to fill every SM at the given occupancy, but
+// no more CTAs than there is work for.
+inline int64_t persistent_grid(int64_t work_ctas, int device, int per_sm) {
+  const int64_t full = static_cast<int64_t>(sm_count(device)) * (per_sm > 0 ? per_sm : 1);
+  return work_ctas < full ? (work_ctas > 0 ? work_ctas : 1) : full;
+}
+
+}  // namespace svllm::k

@@ -1,0 +1,469 @@
+// Qwen3 per-head q/k RMSNorm fused with neox-style rotary embedding, and rotary embedding alone
+// (Llama), in place on q and k, for bf16 and fp32.
+//
+// The reference has no kernel for either: the flags come from small-vLLM src/model/config.h:27-30
+// and config.cpp:34-52, and the formulas are Hugging Face's Qwen3RMSNorm followed by
+// apply_rotary_pos_emb, with cos/sin rounded to the activation dtype as its rotary embedding
+// returns them. One token is one unit: its q row and k row are read from HBM once, normalised
+// per head (Qwen3), rotated, and written back.
+//
+//   * Bulk-copy path (head_dim a multiple of 16 bytes * 2, 16-byte aligned rows): each warp owns
+//     a ring of stages and a contiguous range of tokens; lane 0 keeps cp.async.bulk loads of the
+//     q and k rows of the next tokens in flight. A head belongs to G = head_dim / (2 * vec) lanes,
+//     and lane j of a head holds elements [vec*j, vec*j + vec) and the matching second half, so
+//     every rotation pair (i, i + head_dim/2) is in one lane and the head's sum of squares needs
+//     log2(G) shuffles. The warp computes the token's head_dim/2 (cos, sin) pairs once (two per
+//     lane at head_dim 128), shares them through shared memory, and reuses them for all heads.
+//     inv_freq travels in the kernel parameters (constant bank) and is staged in shared memory.
+//     The angle is one fp32 multiply fp32(pos) * inv_freq[i], as Hugging Face's fp32 outer
+//     product forms it, and cos/sin are the CUDA math library's accurate cosf/sinf (no fast
+//     approximations: their error would grow with the angle), the same functions torch's cos and
+//     sin kernels call, so on one GPU the result equals the torch composite bit for bit.
+//   * Plain path for everything else: one warp per token, element loads, still on the GPU.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cmath>
+#include <cstring>
+
+#include "common.cuh"
+#include "host_common.h"
+
+namespace svllm::k {
+namespace {
+
+constexpr int kMaxHalfDim = 256;  // head_dim <= 512
+
+struct RopeArgs {
+  void* q;
+  void* k;
+  const void* q_weight;
+  const void* k_weight;
+  const void* positions;
+  int64_t num_tokens;
+  int64_t q_stride;  // elements between tokens
+  int64_t k_stride;
+  int num_heads;
+  int num_kv_heads;
+  int head_dim;
+  int pos_is_i64;
+  float eps;
+  int* err;
+  // bulk-copy path
+  int stages;
+  int stage_bytes;
+  int scratch_offset;  // per-warp cos/sin scratch, then the stage rings
+  int ring_offset;
+  float inv_freq[kMaxHalfDim];
+};
+
+__device__ __forceinline__ float load_position(const void* positions, int is_i64, int64_t t) {
+  if (is_i64) {
+    return __ll2float_rn(__ldg(static_cast<const long long*>(positions) + t));
+  }
+  return __int2float_rn(__ldg(static_cast<const int*>(positions) + t));
+}
+
+// Rotation of one lane's pair block: lo[e] = x[i], hi[e] = x[i + d/2] for kVec consecutive i.
+template <class E>
+__device__ __forceinline__ void rotate(float (&lo)[E::kPerVec], float (&hi)[E::kPerVec],
+                                       const float (&c)[E::kPerVec],
+                                       const float (&s)[E::kPerVec]) {
+#pragma unroll
+  for (int e = 0; e < E::kPerVec; ++e) {
+    const float x1 = lo[e];
+    const float x2 = hi[e];
+    lo[e] = __fsub_rn(E::round(__fmul_rn(x1, c[e])), E::round(__fmul_rn(x2, s[e])));
+    hi[e] = __fadd_rn(E::round(__fmul_rn(x2, c[e])), E::round(__fmul_rn(x1, s[e])));
+  }
+}
+
+template <class E, int G, bool kNorm>
+__global__ void __launch_bounds__(256) rope_bulk_kernel(const __grid_constant__ RopeArgs a) {
+  using S = typename E::Storage;
+  constexpr int kVec = E::kPerVec;
+  constexpr int kHalf = kVec * G;  // head_dim / 2
+  constexpr int kDim = 2 * kHalf;
+  constexpr int kHeadsPerPass = kWarpSize / G;
+  extern __shared__ __align__(128) uint8_t smem[];
+
+  const int warps = blockDim.x / kWarpSize;
+  const int warp = threadIdx.x / kWarpSize;
+  const int lane = threadIdx.x % kWarpSize;
+  const int sub = lane % G;
+  const int num_heads = a.num_heads;
+  const int total_heads = a.num_heads + a.num_kv_heads;
+  const uint32_t q_bytes = static_cast<uint32_t>(num_heads) * kDim * sizeof(S);
+  const uint32_t k_bytes = static_cast<uint32_t>(a.num_kv_heads) * kDim * sizeof(S);
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * a.stages;
+  float* inv_sm = reinterpret_cast<float*>(smem + a.scratch_offset);
+  float* cos_sm = inv_sm + kHalf + warp * 2 * kHalf;
+  float* sin_sm = cos_sm + kHalf;
+  uint8_t* ring = smem + a.ring_offset + static_cast<size_t>(warp) * a.stages * a.stage_bytes;
+
+  for (int i = threadIdx.x; i < kHalf; i += blockDim.x) inv_sm[i] = a.inv_freq[i];
+  if (lane == 0) {
+    for (int s = 0; s < a.stages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+
+  // Per-lane norm weights: this lane's block of each half of q_weight and k_weight.
+  float qw_lo[kVec], qw_hi[kVec], kw_lo[kVec], kw_hi[kVec];
+  if constexpr (kNorm) {
+    const uint8_t* qw = static_cast<const uint8_t*>(a.q_weight);
+    const uint8_t* kw = static_cast<const uint8_t*>(a.k_weight);
+    unpack<E>(ld_global_nc_v4(qw + sub * 16), qw_lo);
+    unpack<E>(ld_global_nc_v4(qw + (kHalf * sizeof(S)) + sub * 16), qw_hi);
+    unpack<E>(ld_global_nc_v4(kw + sub * 16), kw_lo);
+    unpack<E>(ld_global_nc_v4(kw + (kHalf * sizeof(S)) + sub * 16), kw_hi);
+  }
+  __syncthreads();
+
+  int64_t t0, t1;
+  partition(a.num_tokens, static_cast<int64_t>(gridDim.x) * warps,
+            static_cast<int64_t>(blockIdx.x) * warps + warp, t0, t1);
+  const int64_t n = t1 - t0;
+  const int64_t q_stride_b = a.q_stride * static_cast<int64_t>(sizeof(S));
+  const int64_t k_stride_b = a.k_stride * static_cast<int64_t>(sizeof(S));
+
+  auto issue = [&](int64_t j) {
+    const int s = static_cast<int>(j % a.stages);
+    uint8_t* st = ring + static_cast<size_t>(s) * a.stage_bytes;
+    const int64_t t = t0 + j;
+    mbar_arrive_expect_tx(&bars[s], q_bytes + k_bytes);
+    if (q_bytes) bulk_load(st, static_cast<const uint8_t*>(a.q) + t * q_stride_b, q_bytes, &bars[s]);
+    if (k_bytes) {
+      bulk_load(st + q_bytes, static_cast<const uint8_t*>(a.k) + t * k_stride_b, k_bytes, &bars[s]);
+    }
+  };
+
+  if (lane == 0) {
+    for (int64_t j = 0; j < min(static_cast<int64_t>(a.stages), n); ++j) issue(j);
+  }
+
+  // Positions run one token ahead of use, so their load latency hides behind a token's work.
+  float pos_next = n > 0 ? load_position(a.positions, a.pos_is_i64, t0) : 0.0f;
+
+  int64_t j = 0;
+  for (; j < n; ++j) {
+    const float pos = pos_next;
+    if (j + 1 < n) pos_next = load_position(a.positions, a.pos_is_i64, t0 + j + 1);
+
+    // The token's (cos, sin) table, shared by every head.
+    for (int i = lane; i < kHalf; i += kWarpSize) {
+      const float angle = __fmul_rn(pos, inv_sm[i]);
+      cos_sm[i] = cosf(angle);
+      sin_sm[i] = sinf(angle);
+    }
+    __syncwarp();
+    float c[kVec], s[kVec];
+#pragma unroll
+    for (int e = 0; e < kVec; ++e) {
+      c[e] = E::round(cos_sm[sub * kVec + e]);
+      s[e] = E::round(sin_sm[sub * kVec + e]);
+    }
+
+    const int stage = static_cast<int>(j % a.stages);
+    const uint32_t parity = static_cast<uint32_t>((j / a.stages) & 1);
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[stage], parity))) break;
+    const uint8_t* st = ring + static_cast<size_t>(stage) * a.stage_bytes;
+    const int64_t t = t0 + j;
+
+    for (int h0 = 0; h0 < total_heads; h0 += kHeadsPerPass) {
+      const int h = h0 + lane / G;
+      const bool valid = h < total_heads;
+      const uint8_t* hs = st + static_cast<size_t>(valid ? h : 0) * kDim * sizeof(S);
+      float lo[kVec], hi[kVec];
+      unpack<E>(ld_shared_v4(hs + sub * 16), lo);
+      unpack<E>(ld_shared_v4(hs + kHalf * sizeof(S) + sub * 16), hi);
+      const bool is_q = h < num_heads;
+      if constexpr (kNorm) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int e = 0; e < kVec; ++e) {
+          ss = __fmaf_rn(lo[e], lo[e], ss);
+          ss = __fmaf_rn(hi[e], hi[e], ss);
+        }
+        ss = group_sum<G>(ss);
+        const float inv_rms = __fdiv_rn(
+            1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(kDim)), a.eps)));
+#pragma unroll
+        for (int e = 0; e < kVec; ++e) {
+          lo[e] = E::round(__fmul_rn(E::round(__fmul_rn(lo[e], inv_rms)), is_q ? qw_lo[e] : kw_lo[e]));
+          hi[e] = E::round(__fmul_rn(E::round(__fmul_rn(hi[e], inv_rms)), is_q ? qw_hi[e] : kw_hi[e]));
+        }
+      }
+      rotate<E>(lo, hi, c, s);
+      if (valid) {
+        S* dst = is_q ? static_cast<S*>(a.q) + t * a.q_stride + static_cast<int64_t>(h) * kDim
+                      : static_cast<S*>(a.k) + t * a.k_stride +
+                            static_cast<int64_t>(h - num_heads) * kDim;
+        st_global_v4(dst + sub * kVec, pack<E>(lo));
+        st_global_v4(dst + kHalf + sub * kVec, pack<E>(hi));
+      }
+    }
+    __syncwarp();
+    if (lane == 0 && j + a.stages < n) {
+      fence_proxy_async_smem();
+      issue(j + a.stages);
+    }
+  }
+
+  if (j < n) {
+    if (lane == 0) {
+      raise_error(a.err, kErrWaitTimeout);
+      for (int64_t m = j; m < min(j + a.stages, n); ++m) {
+        mbar_wait_bounded(&bars[m % a.stages], static_cast<uint32_t>((m / a.stages) & 1));
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// Plain path: one warp per token, any head_dim (even), any alignment.
+template <class E, bool kNorm>
+__global__ void __launch_bounds__(256) rope_plain_kernel(const __grid_constant__ RopeArgs a) {
+  using S = typename E::Storage;
+  const int lane = threadIdx.x % kWarpSize;
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x / kWarpSize);
+  const int dim = a.head_dim;
+  const int half = dim / 2;
+  const int total_heads = a.num_heads + a.num_kv_heads;
+  const S* qw = static_cast<const S*>(a.q_weight);
+  const S* kw = static_cast<const S*>(a.k_weight);
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x / kWarpSize) +
+                   threadIdx.x / kWarpSize;
+       t < a.num_tokens; t += warps_total) {
+    const float pos = load_position(a.positions, a.pos_is_i64, t);
+    for (int h = 0; h < total_heads; ++h) {
+      const bool is_q = h < a.num_heads;
+      S* x = is_q ? static_cast<S*>(a.q) + t * a.q_stride + static_cast<int64_t>(h) * dim
+                  : static_cast<S*>(a.k) + t * a.k_stride + static_cast<int64_t>(h - a.num_heads) * dim;
+      float inv_rms = 1.0f;
+      if constexpr (kNorm) {
+        float ss = 0.0f;
+        for (int i = lane; i < dim; i += kWarpSize) {
+          const float v = E::to_float(x[i]);
+          ss = __fmaf_rn(v, v, ss);
+        }
+        ss = group_sum<kWarpSize>(ss);
+        inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(dim)), a.eps)));
+      }
+      __syncwarp();
+      for (int i = lane; i < half; i += kWarpSize) {
+        float lo[E::kPerVec] = {}, hi[E::kPerVec] = {}, c[E::kPerVec] = {}, s[E::kPerVec] = {};
+        lo[0] = E::to_float(x[i]);
+        hi[0] = E::to_float(x[i + half]);
+        if constexpr (kNorm) {
+          const S* w = is_q ? qw : kw;
+          lo[0] = E::round(__fmul_rn(E::round(__fmul_rn(lo[0], inv_rms)), E::to_float(w[i])));
+          hi[0] = E::round(__fmul_rn(E::round(__fmul_rn(hi[0], inv_rms)), E::to_float(w[i + half])));
+        }
+        const float angle = __fmul_rn(pos, a.inv_freq[i]);
+        c[0] = E::round(cosf(angle));
+        s[0] = E::round(sinf(angle));
+        rotate<E>(lo, hi, c, s);
+        x[i] = E::from_float(lo[0]);
+        x[i + half] = E::from_float(hi[0]);
+      }
+      __syncwarp();
+    }
+  }
+}
+
+template <class E, bool kNorm>
+using RopeKernel = void (*)(RopeArgs);
+
+template <class E, bool kNorm>
+RopeKernel<E, kNorm> pick_bulk_kernel(int head_dim) {
+  constexpr int kVec = E::kPerVec;
+  if (head_dim % (2 * kVec) != 0) return nullptr;
+  switch (head_dim / (2 * kVec)) {
+    case 2: return rope_bulk_kernel<E, 2, kNorm>;
+    case 4: return rope_bulk_kernel<E, 4, kNorm>;
+    case 8: return rope_bulk_kernel<E, 8, kNorm>;
+    case 16: return rope_bulk_kernel<E, 16, kNorm>;
+    case 32: return rope_bulk_kernel<E, 32, kNorm>;
+    default: return nullptr;
+  }
+}
+
+template <class E, bool kNorm>
+int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
+                const void* positions, int pos_type, int64_t num_tokens, int64_t num_heads,
+                int64_t num_kv_heads, int64_t head_dim, int64_t q_stride, int64_t k_stride,
+                float eps, const float* inv_freq, cudaStream_t stream) {
+  using S = typename E::Storage;
+  if (num_tokens < 0 || num_heads < 0 || num_kv_heads < 0 || head_dim <= 0 || head_dim % 2 != 0 ||
+      head_dim > 2 * kMaxHalfDim || (pos_type != SVLLM_INDEX_I32 && pos_type != SVLLM_INDEX_I64) ||
+      (num_heads > 0 && q_stride < num_heads * head_dim) ||
+      (num_kv_heads > 0 && k_stride < num_kv_heads * head_dim) || inv_freq == nullptr) {
+    return SVLLM_ERR_INVALID_ARGUMENT;
+  }
+  if (num_tokens == 0 || num_heads + num_kv_heads == 0) return SVLLM_OK;
+  if (positions == nullptr || (num_heads > 0 && q == nullptr) ||
+      (num_kv_heads > 0 && k == nullptr) ||
+      (kNorm && ((num_heads > 0 && q_weight == nullptr) ||
+                 (num_kv_heads > 0 && k_weight == nullptr)))) {
+    return SVLLM_ERR_INVALID_ARGUMENT;
+  }
+  if (num_heads + num_kv_heads > (1 << 16)) return SVLLM_ERR_TOO_LARGE;
+
+  int device;
+  if (current_device(&device) != SVLLM_OK) return SVLLM_ERR_CUDA;
+  int* err = library_error_word(device);
+  if (err == nullptr) return SVLLM_ERR_CUDA;
+
+  RopeArgs a{};
+  a.q = q;
+  a.k = k;
+  // A missing weight is never read: its heads do not exist. Point it at the other one so the
+  // kernel's unconditional per-lane weight loads stay in bounds.
+  a.q_weight = q_weight != nullptr ? q_weight : k_weight;
+  a.k_weight = k_weight != nullptr ? k_weight : q_weight;
+  a.positions = positions;
+  a.num_tokens = num_tokens;
+  a.q_stride = q_stride;
+  a.k_stride = k_stride;
+  a.num_heads = static_cast<int>(num_heads);
+  a.num_kv_heads = static_cast<int>(num_kv_heads);
+  a.head_dim = static_cast<int>(head_dim);
+  a.pos_is_i64 = pos_type == SVLLM_INDEX_I64;
+  a.eps = eps;
+  a.err = err;
+  std::memcpy(a.inv_freq, inv_freq, sizeof(float) * (head_dim / 2));
+
+  const int64_t head_bytes = head_dim * static_cast<int64_t>(sizeof(S));
+  const int64_t q_bytes = num_heads * head_bytes;
+  const int64_t k_bytes = num_kv_heads * head_bytes;
+  const bool bulk_ok =
+      (num_heads == 0 || (aligned16(q) && (q_stride * sizeof(S)) % 16 == 0)) &&
+      (num_kv_heads == 0 || (aligned16(k) && (k_stride * sizeof(S)) % 16 == 0)) &&
+      (!kNorm || (aligned16(a.q_weight) && aligned16(a.k_weight)));
+  const RopeKernel<E, kNorm> kernel = bulk_ok ? pick_bulk_kernel<E, kNorm>(static_cast<int>(head_dim)) : nullptr;
+  if (kernel != nullptr) {
+    const PipelineShape shape = pipeline_shape(kNorm ? OpId::kQkNormRope : OpId::kRope);
+    a.stage_bytes = static_cast<int>(round_up(q_bytes + k_bytes, 128));
+    int warps = shape.warps;
+    int stages = shape.stages;
+    const int64_t half = head_dim / 2;
+    auto smem_for = [&](int w, int s) {
+      return round_up(static_cast<int64_t>(w) * s * 8, 128) +
+             round_up((half + static_cast<int64_t>(w) * 2 * half) * 4, 128) +
+             static_cast<int64_t>(w) * s * a.stage_bytes;
+    };
+    while (smem_for(warps, stages) > static_cast<int64_t>(kMaxSmemPerCta) && stages > 2) --stages;
+    while (smem_for(warps, stages) > static_cast<int64_t>(kMaxSmemPerCta) && warps > 1) --warps;
+    if (smem_for(warps, stages) <= static_cast<int64_t>(kMaxSmemPerCta) &&
+        q_bytes + k_bytes < (1 << 20)) {
+      a.stages = stages;
+      a.scratch_offset = static_cast<int>(round_up(static_cast<int64_t>(warps) * stages * 8, 128));
+      a.ring_offset = a.scratch_offset +
+                      static_cast<int>(round_up((half + static_cast<int64_t>(warps) * 2 * half) * 4, 128));
+      const size_t smem = static_cast<size_t>(smem_for(warps, stages));
+      const int threads = warps * kWarpSize;
+      const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(kernel), threads, smem, device);
+      if (per_sm > 0) {
+        const int64_t grid = persistent_grid((num_tokens + warps - 1) / warps, device, per_sm);
+        kernel<<<static_cast<unsigned>(grid), threads, smem, stream>>>(a);
+        return launch_status();
+      }
+    }
+  }
+
+  const int64_t grid = persistent_grid((num_tokens + 7) / 8, device, 8);
+  rope_plain_kernel<E, kNorm><<<static_cast<unsigned>(grid), 256, 0, stream>>>(a);
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace svllm::k
+
+using svllm::k::Bf16;
+using svllm::k::F32;
+using svllm::k::launch_rope;
+
+extern "C" {
+
+int svllm_qk_norm_rope_bf16(void* q, void* k, const void* q_weight, const void* k_weight,
+                            const void* positions, int pos_type, int64_t num_tokens,
+                            int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                            int64_t q_row_stride, int64_t k_row_stride, float eps,
+                            const float* inv_freq, svllm_stream stream) {
+  return launch_rope<Bf16, true>(q, k, q_weight, k_weight, positions, pos_type, num_tokens,
+                                 num_heads, num_kv_heads, head_dim, q_row_stride, k_row_stride,
+                                 eps, inv_freq, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int svllm_qk_norm_rope_f32(float* q, float* k, const float* q_weight, const float* k_weight,
+                           const void* positions, int pos_type, int64_t num_tokens,
+                           int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                           int64_t q_row_stride, int64_t k_row_stride, float eps,
+                           const float* inv_freq, svllm_stream stream) {
+  return launch_rope<F32, true>(q, k, q_weight, k_weight, positions, pos_type, num_tokens,
+                                num_heads, num_kv_heads, head_dim, q_row_stride, k_row_stride,
+                                eps, inv_freq, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int svllm_rope_bf16(void* q, void* k, const void* positions, int pos_type, int64_t num_tokens,
+                    int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                    int64_t q_row_stride, int64_t k_row_stride, const float* inv_freq,
+                    svllm_stream stream) {
+  return launch_rope<Bf16, false>(q, k, nullptr, nullptr, positions, pos_type, num_tokens,
+                                  num_heads, num_kv_heads, head_dim, q_row_stride, k_row_stride,
+                                  0.0f, inv_freq, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int svllm_rope_f32(float* q, float* k, const void* positions, int pos_type, int64_t num_tokens,
+                   int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                   int64_t q_row_stride, int64_t k_row_stride, const float* inv_freq,
+                   svllm_stream stream) {
+  return launch_rope<F32, false>(q, k, nullptr, nullptr, positions, pos_type, num_tokens,
+                                 num_heads, num_kv_heads, head_dim, q_row_stride, k_row_stride,
+                                 0.0f, inv_freq, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+extern "C" int svllm_rope_inv_freq(double theta, int64_t head_dim,
+                                   const svllm_llama3_scaling* scaling, float* inv_freq) {
+  // Hugging Face's fp32 formula, one fp32 operation per step. torch evaluates `scalar / tensor`
+  // as reciprocal(tensor) * scalar and `tensor / scalar` as a true division; so does this.
+  if (!(theta > 0.0) || head_dim <= 0 || head_dim % 2 != 0 || inv_freq == nullptr) {
+    return SVLLM_ERR_INVALID_ARGUMENT;
+  }
+  const int64_t half = head_dim / 2;
+  const float base = static_cast<float>(theta);
+  for (int64_t i = 0; i < half; ++i) {
+    const float e = static_cast<float>(2 * i) / static_cast<float>(head_dim);
+    inv_freq[i] = 1.0f / powf(base, e);
+  }
+  if (scaling != nullptr) {
+    const svllm_llama3_scaling& s = *scaling;
+    if (!(s.factor > 0.0) || !(s.high_freq_factor > s.low_freq_factor) ||
+        !(s.low_freq_factor > 0.0) || s.original_max_position_embeddings <= 0) {
+      return SVLLM_ERR_INVALID_ARGUMENT;
+    }
+    const float factor = static_cast<float>(s.factor);
+    const float low = static_cast<float>(s.low_freq_factor);
+    const float old_len = static_cast<float>(s.original_max_position_embeddings);
+    const float low_wavelen =
+        static_cast<float>(static_cast<double>(s.original_max_position_embeddings) / s.low_freq_factor);
+    const float high_wavelen =
+        static_cast<float>(static_cast<double>(s.original_max_position_embeddings) / s.high_freq_factor);
+    const float two_pi = static_cast<float>(2.0 * 3.14159265358979323846);
+    const float span = static_cast<float>(s.high_freq_factor - s.low_freq_factor);
+    for (int64_t i = 0; i < half; ++i) {
+      const float inv = inv_freq[i];
+      const float wavelen = (1.0f / inv) * two_pi;
+      const float scaled = wavelen > low_wavelen ? inv / factor : inv;
+      const float smooth = ((1.0f / wavelen) * old_len - low) / span;
+      const float smoothed = (1.0f - smooth) * scaled / factor + smooth * scaled;
+      const bool medium = !(wavelen < high_wavelen) && !(wavelen > low_wavelen);
+      inv_freq[i] = medium ? smoothed : scaled;
+    }
+  }
+  return SVLLM_OK;
+}

@@ -1,0 +1,240 @@
+// SiLU(gate) * up for bf16 and fp32.
+//
+// The reference has no kernel (planned at small-vLLM docs/ROADMAP.md:40, "SiLU-and-mul"); the
+// formula is Hugging Face's MLP, act_fn(gate_proj(x)) * up_proj(x), evaluated as torch does it:
+// silu(g) = g / (1 + exp(-g)) in fp32 with the CUDA math library's accurate expf and an IEEE
+// division, rounded to the activation dtype, then multiplied by up and rounded again. On one
+// GPU the result therefore equals the torch composite bit for bit.
+//
+//   * Bulk-copy path: the op is elementwise, so a unit is a chunk of columns. When gate, up and
+//     out are all contiguous the whole batch is one flat row and chunks cross row boundaries;
+//     otherwise (gate and up as the two halves of one [rows, 2 * inter] tensor, say) chunks stay
+//     inside a row. Each warp owns a ring of stages; lane 0 keeps cp.async.bulk loads of the
+//     next chunks of gate and up in flight, and the warp writes 16-byte vectors of out.
+//   * Plain path for unaligned or odd-sized rows: grid-stride element loop, still on the GPU.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+
+#include "common.cuh"
+#include "host_common.h"
+
+namespace svllm::k {
+namespace {
+
+struct SiluArgs {
+  void* out;
+  const void* gate;
+  const void* up;
+  int64_t rows;          // rows of the chunked view (1 when the batch is flat)
+  int64_t cols;          // elements per row of the chunked view
+  int64_t out_stride;    // elements
+  int64_t gate_stride;
+  int64_t up_stride;
+  int* err;
+  // bulk-copy path
+  int64_t chunk;         // elements per unit
+  int stages;
+  int stage_bytes;       // gate chunk, then up chunk
+  int ring_offset;
+};
+
+__device__ __forceinline__ float silu(float g) {
+  return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+}
+
+template <class E>
+__global__ void __launch_bounds__(256) silu_bulk_kernel(const SiluArgs a) {
+  using S = typename E::Storage;
+  constexpr int kVec = E::kPerVec;
+  extern __shared__ __align__(128) uint8_t smem[];
+
+  const int warps = blockDim.x / kWarpSize;
+  const int warp = threadIdx.x / kWarpSize;
+  const int lane = threadIdx.x % kWarpSize;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * a.stages;
+  uint8_t* ring = smem + a.ring_offset + static_cast<size_t>(warp) * a.stages * a.stage_bytes;
+  const uint32_t half_stage = static_cast<uint32_t>(a.chunk * sizeof(S));
+
+  if (lane == 0) {
+    for (int s = 0; s < a.stages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+
+  const int64_t chunks_per_row = (a.cols + a.chunk - 1) / a.chunk;
+  const int64_t num_units = a.rows * chunks_per_row;
+  int64_t u0, u1;
+  partition(num_units, static_cast<int64_t>(gridDim.x) * warps,
+            static_cast<int64_t>(blockIdx.x) * warps + warp, u0, u1);
+  const int64_t n = u1 - u0;
+
+  auto unit_of = [&](int64_t u, int64_t& row, int64_t& col, int& len) {
+    row = u / chunks_per_row;
+    col = (u - row * chunks_per_row) * a.chunk;
+    len = static_cast<int>(min(a.chunk, a.cols - col));
+  };
+
+  auto issue = [&](int64_t j) {
+    const int s = static_cast<int>(j % a.stages);
+    uint8_t* st = ring + static_cast<size_t>(s) * a.stage_bytes;
+    int64_t row, col;
+    int len;
+    unit_of(u0 + j, row, col, len);
+    const uint32_t bytes = static_cast<uint32_t>(len) * sizeof(S);
+    mbar_arrive_expect_tx(&bars[s], 2 * bytes);
+    bulk_load(st, static_cast<const S*>(a.gate) + row * a.gate_stride + col, bytes, &bars[s]);
+    bulk_load(st + half_stage, static_cast<const S*>(a.up) + row * a.up_stride + col, bytes,
+              &bars[s]);
+  };
+
+  if (lane == 0) {
+    for (int64_t j = 0; j < min(static_cast<int64_t>(a.stages), n); ++j) issue(j);
+  }
+
+  int64_t j = 0;
+  for (; j < n; ++j) {
+    const int s = static_cast<int>(j % a.stages);
+    const uint32_t parity = static_cast<uint32_t>((j / a.stages) & 1);
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[s], parity))) break;
+    const uint8_t* st = ring + static_cast<size_t>(s) * a.stage_bytes;
+    int64_t row, col;
+    int len;
+    unit_of(u0 + j, row, col, len);
+    S* out = static_cast<S*>(a.out) + row * a.out_stride + col;
+    const int nv = len / kVec;
+    for (int v = lane; v < nv; v += kWarpSize) {
+      float g[kVec], u[kVec];
+      unpack<E>(ld_shared_v4(st + v * 16), g);
+      unpack<E>(ld_shared_v4(st + half_stage + v * 16), u);
+#pragma unroll
+      for (int e = 0; e < kVec; ++e) g[e] = __fmul_rn(E::round(silu(g[e])), u[e]);
+      st_global_v4(out + v * kVec, pack<E>(g));
+    }
+    __syncwarp();
+    if (lane == 0 && j + a.stages < n) {
+      fence_proxy_async_smem();
+      issue(j + a.stages);
+    }
+  }
+
+  if (j < n) {
+    if (lane == 0) {
+      raise_error(a.err, kErrWaitTimeout);
+      for (int64_t m = j; m < min(j + a.stages, n); ++m) {
+        mbar_wait_bounded(&bars[m % a.stages], static_cast<uint32_t>((m / a.stages) & 1));
+      }
+    }
+    __syncwarp();
+  }
+}
+
+template <class E>
+__global__ void __launch_bounds__(256) silu_plain_kernel(const SiluArgs a) {
+  using S = typename E::Storage;
+  const int64_t total = a.rows * a.cols;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += step) {
+    const int64_t row = i / a.cols;
+    const int64_t col = i - row * a.cols;
+    const float g = E::to_float(static_cast<const S*>(a.gate)[row * a.gate_stride + col]);
+    const float u = E::to_float(static_cast<const S*>(a.up)[row * a.up_stride + col]);
+    static_cast<S*>(a.out)[row * a.out_stride + col] =
+        E::from_float(__fmul_rn(E::round(silu(g)), u));
+  }
+}
+
+template <class E>
+int launch_silu(void* out, const void* gate, const void* up, int64_t num_rows, int64_t inter,
+                int64_t out_stride, int64_t gate_stride, int64_t up_stride, cudaStream_t stream) {
+  using S = typename E::Storage;
+  constexpr int kVec = E::kPerVec;
+  if (num_rows < 0 || inter <= 0 || out_stride < inter || gate_stride < inter ||
+      up_stride < inter) {
+    return SVLLM_ERR_INVALID_ARGUMENT;
+  }
+  if (num_rows == 0) return SVLLM_OK;
+  if (out == nullptr || gate == nullptr || up == nullptr) return SVLLM_ERR_INVALID_ARGUMENT;
+
+  int device;
+  if (current_device(&device) != SVLLM_OK) return SVLLM_ERR_CUDA;
+  int* err = library_error_word(device);
+  if (err == nullptr) return SVLLM_ERR_CUDA;
+
+  SiluArgs a{};
+  a.out = out;
+  a.gate = gate;
+  a.up = up;
+  a.err = err;
+  const bool flat = out_stride == inter && gate_stride == inter && up_stride == inter;
+  a.rows = flat ? 1 : num_rows;
+  a.cols = flat ? num_rows * inter : inter;
+  a.out_stride = flat ? 0 : out_stride;
+  a.gate_stride = flat ? 0 : gate_stride;
+  a.up_stride = flat ? 0 : up_stride;
+
+  const bool bulk_ok = aligned16(out) && aligned16(gate) && aligned16(up) && inter % kVec == 0 &&
+                       out_stride % kVec == 0 && gate_stride % kVec == 0 && up_stride % kVec == 0;
+  if (bulk_ok) {
+    const PipelineShape shape = pipeline_shape(OpId::kSiluAndMul);
+    constexpr int64_t kGranule = static_cast<int64_t>(kVec) * kWarpSize;  // one vector per lane
+    int64_t chunk = shape.unit_bytes / (2 * static_cast<int64_t>(sizeof(S)));
+    chunk = std::max<int64_t>(kGranule, chunk / kGranule * kGranule);
+    chunk = std::min<int64_t>(chunk, round_up(a.cols, kVec));
+    a.chunk = chunk;
+    a.stage_bytes = static_cast<int>(round_up(2 * chunk * static_cast<int64_t>(sizeof(S)), 128));
+    int warps = shape.warps;
+    int stages = shape.stages;
+    auto smem_for = [&](int w, int s) {
+      return round_up(static_cast<int64_t>(w) * s * 8, 128) +
+             static_cast<int64_t>(w) * s * a.stage_bytes;
+    };
+    while (smem_for(warps, stages) > static_cast<int64_t>(kMaxSmemPerCta) && stages > 2) --stages;
+    while (smem_for(warps, stages) > static_cast<int64_t>(kMaxSmemPerCta) && warps > 1) --warps;
+    if (smem_for(warps, stages) <= static_cast<int64_t>(kMaxSmemPerCta)) {
+      a.stages = stages;
+      a.ring_offset = static_cast<int>(round_up(static_cast<int64_t>(warps) * stages * 8, 128));
+      const size_t smem = static_cast<size_t>(smem_for(warps, stages));
+      const int threads = warps * kWarpSize;
+      const auto kernel = silu_bulk_kernel<E>;
+      const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(kernel), threads, smem, device);
+      if (per_sm > 0) {
+        const int64_t units = a.rows * ((a.cols + chunk - 1) / chunk);
+        const int64_t grid = persistent_grid((units + warps - 1) / warps, device, per_sm);
+        kernel<<<static_cast<unsigned>(grid), threads, smem, stream>>>(a);
+        return launch_status();
+      }
+    }
+  }
+
+  const int64_t grid = persistent_grid((a.rows * a.cols + 255) / 256, device, 8);
+  silu_plain_kernel<E><<<static_cast<unsigned>(grid), 256, 0, stream>>>(a);
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace svllm::k
+
+using svllm::k::Bf16;
+using svllm::k::F32;
+using svllm::k::launch_silu;
+
+extern "C" {
+
+int svllm_silu_and_mul_bf16(void* out, const void* gate, const void* up, int64_t num_rows,
+                            int64_t inter, int64_t out_row_stride, int64_t gate_row_stride,
+                            int64_t up_row_stride, svllm_stream stream) {
+  return launch_silu<Bf16>(out, gate, up, num_rows, inter, out_row_stride, gate_row_stride,
+                           up_row_stride, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int svllm_silu_and_mul_f32(float* out, const float* gate, const float* up, int64_t num_rows,
+                           int64_t inter, int64_t out_row_stride, int64_t gate_row_stride,
+                           int64_t up_row_stride, svllm_stream stream) {
+  return launch_silu<F32>(out, gate, up, num_rows, inter, out_row_stride, gate_row_stride,
+                          up_row_stride, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,305 @@
+"""Parity of the sm_100a kernels, called through the C ABI (svllm_capi), with the oracle
+(oracle/, the C/OpenMP restatement) on the same seeded inputs, for bf16 and fp32, across the
+bulk-copy path, the plain-load path (unaligned or odd sizes), strided rows and the edge cases.
+
+Bars (the north star's tolerances, written per test):
+  * embedding: bit-exact.
+  * fp32 outputs: within 1e-5 relative of the oracle.
+  * bf16 outputs: within 1 bf16 ulp of the oracle for the norms (the GPU sums squares in fp32 in
+    a tree, the oracle in double), bit-exact for the residual add; rotary outputs within one bf16
+    rounding of each rotation term (the C library's cosf/sinf are not CUDA's), and bit-exact
+    against the torch composite on the same GPU, which calls the same CUDA functions; SiLU-mul
+    within 2 ulp of the oracle (expf differs by an fp32 ulp between the two libraries, which can
+    move the rounded SiLU by one step) and bit-exact against torch on the GPU.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle
+import svllm_capi as capi
+from conftest import (assert_bf16_within_ulp, assert_rel_f32, bf16_values, from_bits, random_t,
+                      to_bits)
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = [torch.bfloat16, torch.float32]
+
+
+def ids_of(dt):
+    return "bf16" if dt == torch.bfloat16 else "f32"
+
+
+def np_of(t: torch.Tensor) -> np.ndarray:
+    return to_bits(t)
+
+
+def check(ours: torch.Tensor, ref: np.ndarray, dt, max_ulp: int, what: str, min_exact=0.99):
+    if dt == torch.bfloat16:
+        exact = assert_bf16_within_ulp(ours, ref, max_ulp, what)
+        assert exact >= min_exact, f"{what}: only {exact:.4%} bit-exact"
+    else:
+        assert_rel_f32(ours, ref, 1e-5, what)
+
+
+@pytest.fixture(autouse=True)
+def _clear_device_error(cuda):
+    capi.read_device_error(0, reset=True)
+    yield
+    torch.cuda.synchronize()
+    assert capi.read_device_error(0, reset=True) & capi.DEVERR_WAIT_TIMEOUT == 0
+
+
+# ---------------------------------------------------------------------------------------------
+# rms_norm
+
+RMS_SHAPES = [(1, 128), (4, 64), (7, 1024), (50, 2048), (3, 4100), (2, 16384), (300, 1024),
+              (4096, 128), (2049, 1024), (1000, 768), (33, 4096)]
+
+
+@pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
+@pytest.mark.parametrize("shape", RMS_SHAPES, ids=str)
+def test_rms_norm(cuda, dt, shape):
+    x = random_t(*shape, dtype=dt, device=cuda, seed=1)
+    w = random_t(shape[-1], dtype=dt, device=cuda, seed=2, scale=0.1, shift=1.0)
+    out = torch.empty_like(x)
+    capi.rms_norm(out, x, w, 1e-6)
+    ref = oracle.rms_norm(np_of(x), np_of(w), 1e-6)
+    check(out, ref, dt, 1, f"rms_norm {shape}")
+
+
+@pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
+def test_rms_norm_strided_and_unaligned(cuda, dt):
+    rows, hidden = 37, 1024
+    big = random_t(rows, hidden + 8, dtype=dt, device=cuda, seed=3)
+    x = big[:, :hidden]  # row stride hidden + 8: still 16-byte aligned rows
+    w = random_t(hidden, dtype=dt, device=cuda, seed=4)
+    out_big = torch.zeros(rows, hidden + 16, dtype=dt, device=cuda)
+    out = out_big[:, 8:8 + hidden]
+    capi.rms_norm(out, x, w, 1e-5)
+    ref = oracle.rms_norm(np_of(x.contiguous()), np_of(w), 1e-5)
+    check(out.contiguous(), ref, dt, 1, "strided")
+    assert not out_big[:, :8].any() and not out_big[:, 8 + hidden:].any(), "wrote outside rows"
+    # one element in: rows lose 16-byte alignment, the plain-load path runs
+    flat = random_t(rows * hidden + 1, dtype=dt, device=cuda, seed=5)
+    xu = flat[1:].view(rows, hidden)
+    outu = torch.empty_like(xu)
+    capi.rms_norm(outu, xu, w, 1e-5)
+    check(outu, oracle.rms_norm(np_of(xu), np_of(w), 1e-5), dt, 1, "unaligned")
+
+
+# ---------------------------------------------------------------------------------------------
+# add_rms_norm
+
+@pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
+@pytest.mark.parametrize("shape", [(1, 1024), (7, 1024), (1000, 1024), (513, 2048), (5, 4100),
+                                   (64, 128)], ids=str)
+def test_add_rms_norm(cuda, dt, shape):
+    x = random_t(*shape, dtype=dt, device=cuda, seed=6)
+    r = random_t(*shape, dtype=dt, device=cuda, seed=7)
+    w = random_t(shape[-1], dtype=dt, device=cuda, seed=8, scale=0.1, shift=1.0)
+    ref_x, ref_r = oracle.add_rms_norm(np_of(x), np_of(r), np_of(w), 1e-6)
+    capi.add_rms_norm(x, r, w, 1e-6)
+    assert np.array_equal(np_of(r), ref_r), "residual + x must be bit-exact"
+    check(x, ref_x, dt, 1, f"add_rms_norm {shape}")
+
+
+# ---------------------------------------------------------------------------------------------
+# rotary embedding
+
+def rope_bound_ok(out, ref, pre) -> np.ndarray:
+    """Within one bf16 rounding of each rotation term, plus one of the result."""
+    o = bf16_values(out).astype(np.float64)
+    r = bf16_values(ref).astype(np.float64)
+    p = bf16_values(pre).astype(np.float64)
+    half = p.shape[-1] // 2
+    mag = np.abs(p[..., :half]) + np.abs(p[..., half:])
+    mag = np.concatenate([mag, mag], axis=-1)
+    return np.abs(o - r) <= 2.0 ** -7 * mag + 2.0 ** -8 * np.abs(r) + 1e-30
+
+
+def torch_rope(x, pos, inv):
+    """Hugging Face's rotary embedding as torch ops, on x's device."""
+    freqs = pos.float()[:, None] * inv.to(x.device)[None, :]
+    emb = torch.cat((freqs, freqs), dim=-1)
+    cos, sin = emb.cos().to(x.dtype)[:, None, :], emb.sin().to(x.dtype)[:, None, :]
+    half = x.shape[-1] // 2
+    return x * cos + torch.cat((-x[..., half:], x[..., :half]), dim=-1) * sin
+
+
+def _positions(T, hi, dtype, cuda, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, hi, (T,), generator=g).to(device=cuda, dtype=dtype)
+
+
+@pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
+@pytest.mark.parametrize("T, hq, hk, d, pos_dtype", [
+    (1, 16, 8, 128, torch.int64), (7, 16, 8, 128, torch.int32), (256, 16, 8, 128, torch.int64),
+    (2000, 16, 8, 128, torch.int64), (300, 32, 8, 64, torch.int32), (40, 8, 2, 256, torch.int64),
+    (20, 4, 2, 96, torch.int64), (11, 4, 1, 32, torch.int32),
+], ids=str)
+def test_qk_norm_rope(cuda, dt, T, hq, hk, d, pos_dtype):
+    q = random_t(T, hq, d, dtype=dt, device=cuda, seed=9)
+    k = random_t(T, hk, d, dtype=dt, device=cuda, seed=10)
+    qw = random_t(d, dtype=dt, device=cuda, seed=11, scale=0.1, shift=1.0)
+    kw = random_t(d, dtype=dt, device=cuda, seed=12, scale=0.1, shift=1.0)
+    pos = _positions(T, 32768, pos_dtype, cuda, 13)
+    inv = oracle.inv_freq(1e6, d)
+    rq, rk = oracle.qk_norm_rope(np_of(q), np_of(k), np_of(qw), np_of(kw), np_of(pos).astype(
+        np.int64 if pos_dtype == torch.int64 else np.int32), 1e-6, inv)
+    pre_q = oracle.rms_norm(np_of(q).reshape(-1, d), np_of(qw), 1e-6).reshape(q.shape)
+    pre_k = oracle.rms_norm(np_of(k).reshape(-1, d), np_of(kw), 1e-6).reshape(k.shape)
+    capi.qk_norm_rope(q, k, qw, kw, pos, 1e-6, inv)
+    if dt == torch.bfloat16:
+        assert rope_bound_ok(q, rq, pre_q).all() and rope_bound_ok(k, rk, pre_k).all()
+        assert (np_of(q) == rq).mean() > 0.99
+    else:
+        assert_rel_f32(q, rq, 1e-5, "q")
+        assert_rel_f32(k, rk, 1e-5, "k")
+
+
+@pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
+@pytest.mark.parametrize("factor", [8.0, 32.0])
+def test_llama3_rope(cuda, dt, factor):
+    T, hq, hk, d = 1000, 32, 8, 64
+    q = random_t(T, hq, d, dtype=dt, device=cuda, seed=14)
+    k = random_t(T, hk, d, dtype=dt, device=cuda, seed=15)
+    pos = (torch.arange(T, device=cuda) % 2048)
+    inv = oracle.inv_freq(5e5, d, (factor, 1.0, 4.0, 8192))
+    invt = torch.from_numpy(inv)
+    eq, ek = torch_rope(q, pos, invt), torch_rope(k, pos, invt)
+    rq, rk = oracle.rope(np_of(q), np_of(k), np_of(pos), inv)
+    pq, pk = np_of(q).copy(), np_of(k).copy()
+    capi.rope(q, k, pos, inv)
+    if dt == torch.bfloat16:
+        # same GPU, same cosf/sinf as the torch composite: bit-exact
+        assert torch.equal(q, eq) and torch.equal(k, ek)
+        assert rope_bound_ok(q, rq, pq).all() and rope_bound_ok(k, rk, pk).all()
+    else:
+        assert_rel_f32(q, rq, 1e-5, "q")
+        assert_rel_f32(k, rk, 1e-5, "k")
+        torch.testing.assert_close(q, eq, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
+def test_rope_on_strided_views(cuda, dt):
+    T, hq, hk, d = 129, 16, 8, 128
+    qkv = random_t(T, (hq + 2 * hk) * d, dtype=dt, device=cuda, seed=16)
+    q = qkv[:, : hq * d].view(T, hq, d)
+    k = qkv[:, hq * d:(hq + hk) * d].view(T, hk, d)
+    v_before = qkv[:, (hq + hk) * d:].clone()
+    pos = torch.arange(T, device=cuda, dtype=torch.int32) * 7
+    inv = oracle.inv_freq(1e6, d)
+    rq, rk = oracle.rope(np_of(q.contiguous()), np_of(k.contiguous()), np_of(pos), inv)
+    capi.rope(q, k, pos, inv)
+    check(q.contiguous(), rq, dt, 1, "q view", min_exact=0.99)
+    check(k.contiguous(), rk, dt, 1, "k view", min_exact=0.99)
+    assert torch.equal(qkv[:, (hq + hk) * d:], v_before)
+
+
+# ---------------------------------------------------------------------------------------------
+# silu_and_mul
+
+@pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
+@pytest.mark.parametrize("shape", [(1, 3072), (7, 3072), (1000, 3072), (33, 8192), (3, 3001),
+                                   (5, 64)], ids=str)
+def test_silu_and_mul(cuda, dt, shape):
+    gate = random_t(*shape, dtype=dt, device=cuda, seed=17, scale=3.0)
+    up = random_t(*shape, dtype=dt, device=cuda, seed=18)
+    out = torch.empty_like(gate)
+    capi.silu_and_mul(out, gate, up)
+    ref = oracle.silu_and_mul(np_of(gate), np_of(up))
+    check(out, ref, dt, 2, f"silu_and_mul {shape}")
+    if dt == torch.bfloat16:
+        assert torch.equal(out, F.silu(gate) * up), "same GPU, same expf: bit-exact with torch"
+
+
+@pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
+def test_silu_and_mul_halves(cuda, dt):
+    rows, inter = 77, 3072
+    gate_up = random_t(rows, 2 * inter, dtype=dt, device=cuda, seed=19, scale=2.0)
+    gate, up = gate_up[:, :inter], gate_up[:, inter:]
+    out = torch.empty(rows, inter, dtype=dt, device=cuda)
+    capi.silu_and_mul(out, gate, up)
+    check(out, oracle.silu_and_mul(np_of(gate.contiguous()), np_of(up.contiguous())), dt, 2,
+          "halves")
+
+
+# ---------------------------------------------------------------------------------------------
+# embedding
+
+@pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
+@pytest.mark.parametrize("T, vocab, hidden, ids_dtype", [
+    (1, 151936, 1024, torch.int32), (33, 151936, 1024, torch.int64),
+    (5000, 151936, 1024, torch.int32), (777, 128256, 2048, torch.int64),
+    (100, 1000, 1001, torch.int32),  # odd row size: plain path
+], ids=str)
+def test_embedding(cuda, dt, T, vocab, hidden, ids_dtype):
+    table = random_t(vocab, hidden, dtype=dt, device=cuda, seed=20, scale=0.02)
+    g = torch.Generator().manual_seed(21)
+    ids = torch.randint(0, vocab, (T,), generator=g).to(device=cuda, dtype=ids_dtype)
+    out = torch.empty(T, hidden, dtype=dt, device=cuda)
+    capi.embedding(out, ids, table)
+    assert torch.equal(out, table[ids.long()])
+    ref, bad = oracle.embedding(np_of(ids), np_of(table))
+    assert bad == 0 and np.array_equal(np_of(out), ref)
+
+
+def test_embedding_bad_ids_zero_rows_and_raise_the_error_word(cuda):
+    vocab, hidden = 4000, 1024
+    table = random_t(vocab, hidden, device=cuda, seed=22)
+    ids = torch.tensor([3, -1, vocab, 17, vocab + 1000, 0], device=cuda, dtype=torch.int64)
+    out = torch.full((6, hidden), 7.0, dtype=torch.bfloat16, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    capi.embedding(out, ids, table, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & capi.DEVERR_BAD_INDEX
+    for i, good in enumerate([True, False, False, True, False, True]):
+        if good:
+            assert torch.equal(out[i], table[ids[i]])
+        else:
+            assert not out[i].any()
+    # with no err pointer the library's own word records it
+    capi.embedding(out, ids, table)
+    assert capi.read_device_error(0, reset=True) & capi.DEVERR_BAD_INDEX
+
+
+def test_embedding_strided_output_rows(cuda):
+    vocab, hidden, T = 5000, 1024, 300
+    table = random_t(vocab, hidden, device=cuda, seed=23)
+    ids = torch.randint(0, vocab, (T,), device=cuda)
+    big = torch.zeros(T, hidden + 64, dtype=torch.bfloat16, device=cuda)
+    out = big[:, 32:32 + hidden]
+    capi.embedding(out, ids, table)
+    assert torch.equal(out, table[ids])
+    assert not big[:, :32].any() and not big[:, 32 + hidden:].any()
+
+
+# ---------------------------------------------------------------------------------------------
+# pipeline shapes do not change results
+
+@pytest.mark.parametrize("unit, stages, warps", [(2048, 2, 1), (4096, 3, 8), (16384, 4, 2)])
+def test_pipeline_shape_does_not_change_results(cuda, unit, stages, warps):
+    x = random_t(999, 1024, device=cuda, seed=24)
+    w = random_t(1024, device=cuda, seed=25)
+    base = torch.empty_like(x)
+    capi.rms_norm(base, x, w, 1e-6)
+    gate = random_t(50, 3072, device=cuda, seed=26)
+    up = random_t(50, 3072, device=cuda, seed=27)
+    sbase = torch.empty_like(gate)
+    capi.silu_and_mul(sbase, gate, up)
+    try:
+        for op in ("rms_norm", "silu_and_mul"):
+            capi.set_pipeline(op, unit, stages, warps)
+        out = torch.empty_like(x)
+        capi.rms_norm(out, x, w, 1e-6)
+        sout = torch.empty_like(gate)
+        capi.silu_and_mul(sout, gate, up)
+    finally:
+        for op in ("rms_norm", "silu_and_mul"):
+            capi.set_pipeline(op, 8192, 4, 4)
+    assert torch.equal(out, base) and torch.equal(sout, sbase)

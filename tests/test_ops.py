@@ -1,0 +1,201 @@
+"""svllm_ops' fused layer ops against torch composites of the Hugging Face formulas, on CPU (the
+OpenMP backend) and CUDA (the sm_100a kernels, marked gpu), in the reference's op-test style
+(parametrized shapes, seeded inputs, its bf16 tolerance) plus argument checks."""
+
+from __future__ import annotations
+
+import pytest
+import svllm_ops
+import torch
+import torch.nn.functional as F
+from conftest import assert_close_bf16, random_bf16, random_t
+
+QWEN_EPS = 1e-6
+LLAMA3 = (8.0, 1.0, 4.0, 8192)
+
+
+def hf_rms_norm(x, w, eps):
+    """Qwen3RMSNorm: fp32 normalise, round to x's dtype, multiply by the weight."""
+    xf = x.float()
+    var = xf.pow(2).mean(-1, keepdim=True)
+    return w * (xf * torch.rsqrt(var + eps)).to(x.dtype)
+
+
+def hf_rope(x, pos, inv_freq):
+    """apply_rotary_pos_emb on [T, H, D] with Hugging Face's fp32 angles and bf16 cos/sin."""
+    freqs = pos.float()[:, None] * inv_freq.to(x.device)[None, :]
+    emb = torch.cat((freqs, freqs), dim=-1)
+    cos, sin = emb.cos().to(x.dtype)[:, None, :], emb.sin().to(x.dtype)[:, None, :]
+    half = x.shape[-1] // 2
+    rot = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+    return x * cos + rot * sin
+
+
+# ---------------------------------------------------------------------------------------------
+# add_rms_norm
+
+@pytest.mark.parametrize("shape", [(1, 1024), (7, 1024), (300, 1024), (5, 2048), (3, 4100),
+                                   (0, 1024)], ids=str)
+def test_add_rms_norm(device, shape):
+    x = random_bf16(*shape, device=device, seed=3)
+    r = random_bf16(*shape, device=device, seed=4)
+    w = random_t(shape[-1], device=device, seed=5, scale=0.1, shift=1.0)
+    expected_r = x + r
+    expected_x = hf_rms_norm(expected_r, w, QWEN_EPS)
+    svllm_ops.add_rms_norm(x, r, w, QWEN_EPS)
+    assert torch.equal(r, expected_r), "the residual add is one bf16 rounding: bit-exact"
+    assert_close_bf16(x, expected_x)
+
+
+def test_add_rms_norm_rejects_mismatch():
+    x = torch.ones(2, 8, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="do not match"):
+        svllm_ops.add_rms_norm(x, torch.ones(2, 4, dtype=torch.bfloat16),
+                               torch.ones(8, dtype=torch.bfloat16), 1e-6)
+    with pytest.raises(RuntimeError, match="expected bf16"):
+        svllm_ops.add_rms_norm(x.float(), x, torch.ones(8, dtype=torch.bfloat16), 1e-6)
+    with pytest.raises(RuntimeError, match="unsupported device"):
+        m = torch.ones(2, 8, dtype=torch.bfloat16, device="meta")
+        svllm_ops.add_rms_norm(m, m, torch.ones(8, dtype=torch.bfloat16, device="meta"), 1e-6)
+
+
+# ---------------------------------------------------------------------------------------------
+# qk_norm_rope (Qwen3) and rope (Llama)
+
+@pytest.mark.parametrize("T, pos_dtype", [(1, torch.int64), (7, torch.int32), (64, torch.int64)])
+def test_qk_norm_rope(device, T, pos_dtype):
+    q = random_bf16(T, 16, 128, device=device, seed=6)
+    k = random_bf16(T, 8, 128, device=device, seed=7)
+    qw = random_t(128, device=device, seed=8, scale=0.1, shift=1.0)
+    kw = random_t(128, device=device, seed=9, scale=0.1, shift=1.0)
+    g = torch.Generator().manual_seed(10)
+    pos = torch.randint(0, 32768, (T,), generator=g).to(device=device, dtype=pos_dtype)
+    inv = svllm_ops.rope_inv_freq(1e6, 128)
+    eq = hf_rope(hf_rms_norm(q, qw, QWEN_EPS), pos, inv)
+    ek = hf_rope(hf_rms_norm(k, kw, QWEN_EPS), pos, inv)
+    svllm_ops.qk_norm_rope(q, k, qw, kw, pos, QWEN_EPS, 1e6)
+    assert_close_bf16(q, eq, atol=2e-2)
+    assert_close_bf16(k, ek, atol=2e-2)
+
+
+@pytest.mark.parametrize("factor", [8.0, 32.0])
+def test_llama3_rope(device, factor):
+    T = 33
+    q = random_bf16(T, 32, 64, device=device, seed=11)
+    k = random_bf16(T, 8, 64, device=device, seed=12)
+    pos = torch.arange(T, device=device) * 61
+    scaling = svllm_ops.Llama3RopeScaling(factor, 1.0, 4.0, 8192)
+    inv = svllm_ops.rope_inv_freq(5e5, 64, scaling)
+    eq, ek = hf_rope(q, pos, inv), hf_rope(k, pos, inv)
+    svllm_ops.rope(q, k, pos, 5e5, scaling)
+    assert_close_bf16(q, eq, atol=2e-2)
+    assert_close_bf16(k, ek, atol=2e-2)
+
+
+def test_rope_on_views_of_a_fused_qkv_tensor(device):
+    T, hq, hk, d = 9, 16, 8, 128
+    qkv = random_bf16(T, (hq + 2 * hk) * d, device=device, seed=13)
+    q = qkv[:, : hq * d].view(T, hq, d)
+    k = qkv[:, hq * d:(hq + hk) * d].view(T, hk, d)
+    v_before = qkv[:, (hq + hk) * d:].clone()
+    pos = torch.arange(T, device=device)
+    inv = svllm_ops.rope_inv_freq(1e6, d)
+    eq, ek = hf_rope(q.clone(), pos, inv), hf_rope(k.clone(), pos, inv)
+    svllm_ops.rope(q, k, pos, 1e6)
+    assert_close_bf16(q, eq, atol=2e-2)
+    assert_close_bf16(k, ek, atol=2e-2)
+    assert torch.equal(qkv[:, (hq + hk) * d:], v_before), "v must be untouched"
+
+
+def test_rope_inv_freq_is_hugging_face_bit_for_bit():
+    from conftest import golden
+
+    g = golden()
+    assert torch.equal(svllm_ops.rope_inv_freq(1e6, 128),
+                       torch.from_numpy(g["inv_freq/qwen3"]))
+    for factor, name in ((8.0, "llama3"), (32.0, "llama3_f32x")):
+        s = svllm_ops.Llama3RopeScaling(factor, 1.0, 4.0, 8192)
+        assert torch.equal(svllm_ops.rope_inv_freq(5e5, 64, s), torch.from_numpy(g[f"inv_freq/{name}"]))
+
+
+def test_rope_rejects_bad_inputs():
+    q = torch.ones(2, 4, 8, dtype=torch.bfloat16)
+    k = torch.ones(2, 2, 8, dtype=torch.bfloat16)
+    pos = torch.arange(2)
+    with pytest.raises(RuntimeError, match="expected bf16"):
+        svllm_ops.rope(q.float(), k, pos, 1e4)
+    with pytest.raises(RuntimeError, match="int32 or int64"):
+        svllm_ops.rope(q, k, pos.float(), 1e4)
+    with pytest.raises(RuntimeError, match="positions for"):
+        svllm_ops.rope(q, k, torch.arange(3), 1e4)
+    with pytest.raises(RuntimeError, match="do not match"):
+        svllm_ops.rope(q, torch.ones(2, 2, 6, dtype=torch.bfloat16), pos, 1e4)
+    with pytest.raises(RuntimeError, match="even"):
+        svllm_ops.rope(torch.ones(2, 4, 7, dtype=torch.bfloat16),
+                       torch.ones(2, 2, 7, dtype=torch.bfloat16), pos, 1e4)
+    with pytest.raises(RuntimeError, match="contiguous heads"):
+        svllm_ops.rope(torch.ones(2, 8, 4, dtype=torch.bfloat16).transpose(1, 2), k, pos, 1e4)
+    with pytest.raises(RuntimeError, match="unsupported device"):
+        m = lambda t: t.to("meta")  # noqa: E731
+        svllm_ops.rope(m(q), m(k), m(pos), 1e4)
+
+
+# ---------------------------------------------------------------------------------------------
+# silu_and_mul
+
+@pytest.mark.parametrize("shape", [(1, 3072), (7, 3072), (130, 8192), (3, 3001), (0, 3072),
+                                   (2, 3, 256)], ids=str)
+def test_silu_and_mul(device, shape):
+    gate = random_bf16(*shape, device=device, seed=14) * 3
+    up = random_bf16(*shape, device=device, seed=15)
+    expected = F.silu(gate) * up
+    out = svllm_ops.silu_and_mul(gate, up)
+    assert out.shape == gate.shape and out.is_contiguous()
+    assert_close_bf16(out, expected)
+
+
+def test_silu_and_mul_on_halves_of_a_gate_up_projection(device):
+    gate_up = random_bf16(17, 2 * 3072, device=device, seed=16)
+    gate, up = gate_up[:, :3072], gate_up[:, 3072:]
+    assert_close_bf16(svllm_ops.silu_and_mul(gate, up), F.silu(gate) * up)
+
+
+def test_silu_and_mul_rejects_bad_inputs():
+    a = torch.ones(2, 8, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="expected bf16"):
+        svllm_ops.silu_and_mul(a.float(), a)
+    with pytest.raises(RuntimeError, match="does not match"):
+        svllm_ops.silu_and_mul(a, torch.ones(2, 4, dtype=torch.bfloat16))
+    with pytest.raises(RuntimeError, match="contiguous last"):
+        svllm_ops.silu_and_mul(torch.ones(8, 2, dtype=torch.bfloat16).t(), a)
+
+
+# ---------------------------------------------------------------------------------------------
+# embedding
+
+@pytest.mark.parametrize("ids_dtype", [torch.int32, torch.int64])
+@pytest.mark.parametrize("shape", [(1,), (37,), (4, 9), (0,)], ids=str)
+def test_embedding(device, ids_dtype, shape):
+    vocab, hidden = 1000, 1024
+    table = random_t(vocab, hidden, device=device, seed=17, scale=0.02)
+    g = torch.Generator().manual_seed(18)
+    ids = torch.randint(0, vocab, shape, generator=g).to(device=device, dtype=ids_dtype)
+    out = svllm_ops.embedding(ids, table)
+    assert out.shape == (*shape, hidden)
+    assert torch.equal(out, F.embedding(ids.long(), table)), "the gather is bit-exact"
+
+
+def test_embedding_out_of_range_ids_fail_on_cpu():
+    table = torch.ones(10, 16, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="ids outside"):
+        svllm_ops.embedding(torch.tensor([1, 10, -1]), table)
+
+
+def test_embedding_rejects_bad_inputs():
+    table = torch.ones(10, 16, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="int32 or int64"):
+        svllm_ops.embedding(torch.tensor([1.0]), table)
+    with pytest.raises(RuntimeError, match="bf16 table"):
+        svllm_ops.embedding(torch.tensor([1]), table.float())
+    with pytest.raises(RuntimeError, match="vocab, hidden"):
+        svllm_ops.embedding(torch.tensor([1]), torch.ones(16, dtype=torch.bfloat16))
