@@ -474,89 +474,69 @@ def load_traffic(kernel_op: str, tokens: int):
 
 
 # ---------------------------------------------------------------------------------------------
-# Validation (outside every timed region): a sample of each rank's rows is checked against the
-# oracle after an NCCL all-gather of the output shards to rank 0.
+# Validation (outside every timed region): the first rows of every rank's shard, inputs and
+# outputs, are all-gathered to rank 0 (NCCL, the one collective of the sharded run) and recomputed
+# there by svllm_ops' CPU backend. The embedding and the residual add must agree bit for bit;
+# the other outputs within 2 bf16 ulp, or within 2^-7 of their row's largest magnitude where a
+# rotation cancels (the CPU's cosf/sinf/expf are the C library's, not CUDA's).
 
 def validate(chain, inp, cfg, world, rank, dev, rows: int = 256):
     import numpy as np
     import torch
     import torch.distributed as dist
 
-    import oracle
+    import svllm_dist
+    import svllm_ops
 
     n = min(rows, inp["ids"].shape[0])
-
-    def bits(t):
-        return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
-
+    if world > 1:
+        t = torch.tensor([n], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        n = int(t.item())
     saved = {k: inp[k][:n].clone() for k in ("ids", "x", "residual", "q", "k", "pos", "gate",
                                             "up")}
     for op in OPS:
         chain.run_op(op)
     torch.cuda.synchronize()
-    outs = [chain.emb_out[:n], inp["x"][:n], inp["residual"][:n], inp["q"][:n].reshape(n, -1),
-            inp["k"][:n].reshape(n, -1), chain.silu_out[:n]]
-    packed = torch.cat([o.reshape(n, -1) for o in outs], dim=1).contiguous()
-    ins = torch.cat([saved[k].reshape(n, -1).view(torch.int16)
-                     for k in ("x", "residual", "q", "k", "gate", "up")], dim=1).contiguous()
-    ids_pos = torch.stack([saved["ids"].to(torch.int64), saved["pos"]], dim=1).contiguous()
-    if world > 1:
-        g_out = [torch.empty_like(packed) for _ in range(world)]
-        g_in = [torch.empty_like(ins) for _ in range(world)]
-        g_ip = [torch.empty_like(ids_pos) for _ in range(world)]
-        dist.all_gather(g_out, packed)
-        dist.all_gather(g_in, ins)
-        dist.all_gather(g_ip, ids_pos)
-    else:
-        g_out, g_in, g_ip = [packed], [ins], [ids_pos]
+    got = {"embedding": chain.emb_out[:n], "x": inp["x"][:n], "residual": inp["residual"][:n],
+           "q": inp["q"][:n], "k": inp["k"][:n], "silu": chain.silu_out[:n]}
+
+    def gather(t):
+        return svllm_dist.all_gather_rows(t.contiguous(), n * world) if world > 1 else t
+
+    got = {k: gather(v).cpu() for k, v in got.items()}
+    ins = {k: gather(v).cpu() for k, v in saved.items()}
     if rank != 0:
         return None
-    h, hd, inter = cfg["hidden"], cfg["head_dim"], cfg["inter"]
-    nq, nk = cfg["heads"] * hd, cfg["kv_heads"] * hd
-    table = bits(inp["table"])
-    inv = svllm_inv(cfg)
-    worst = 0
-    mismatched = 0
-    for r in range(world):
-        o = bits(g_out[r].view(torch.bfloat16))
-        i = g_in[r].cpu().numpy().view(np.uint16)
-        ip = g_ip[r].cpu().numpy()
-        x, res = i[:, :h], i[:, h:2 * h]
-        q, k = i[:, 2 * h:2 * h + nq], i[:, 2 * h + nq:2 * h + nq + nk]
-        gate = i[:, 2 * h + nq + nk:2 * h + nq + nk + inter]
-        up = i[:, 2 * h + nq + nk + inter:]
-        emb, bad = oracle.embedding(ip[:, 0].astype(np.int32), table)
-        ox, orr = oracle.add_rms_norm(x, res, bits(inp["w"]), cfg["eps"])
-        oq, ok = oracle.qk_norm_rope(q.reshape(n, -1, hd), k.reshape(n, -1, hd), bits(inp["qw"]),
-                                     bits(inp["kw"]), ip[:, 1], cfg["eps"], inv)
-        oy = oracle.silu_and_mul(gate, up)
-        col = 0
-        for name, ref, width in (("embedding", emb, h), ("x", ox, h), ("residual", orr, h),
-                                 ("q", oq.reshape(n, -1), nq), ("k", ok.reshape(n, -1), nk),
-                                 ("silu", oy, inter)):
-            got = o[:, col:col + width]
-            col += width
-            d = np.abs(key(got) - key(ref))
-            worst = max(worst, int(d.max()))
-            mismatched += int((d > 0).sum())
-        if bad:
-            worst = max(worst, 1 << 20)
-    return {"rows_per_gpu": n, "gathered_from": world, "worst_bf16_ulp": worst,
-            "elements_not_bit_exact": mismatched,
-            "ok": worst <= 2}
 
+    ops = svllm_ops
+    emb = ops.embedding(ins["ids"], inp["table"].cpu())
+    x, r = ins["x"].clone(), ins["residual"].clone()
+    ops.add_rms_norm(x, r, inp["w"].cpu(), cfg["eps"])
+    q, k = ins["q"].clone(), ins["k"].clone()
+    ops.qk_norm_rope(q, k, inp["qw"].cpu(), inp["kw"].cpu(), ins["pos"], cfg["eps"], cfg["theta"])
+    y = ops.silu_and_mul(ins["gate"], ins["up"])
+    want = {"embedding": emb, "x": x, "residual": r, "q": q, "k": k, "silu": y}
 
-def key(bits_arr):
-    import numpy as np
+    def bits(t):
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16).astype(np.int32)
 
-    b = bits_arr.astype(np.int32)
-    return np.where(b & 0x8000, -(b & 0x7FFF), b)
-
-
-def svllm_inv(cfg):
-    import svllm_ops
-
-    return svllm_ops.rope_inv_freq(cfg["theta"], cfg["head_dim"]).numpy()
+    report, ok = {}, True
+    for name in want:
+        a, b = bits(got[name]), bits(want[name])
+        ulp = np.abs(np.where(a & 0x8000, -(a & 0x7FFF), a) - np.where(b & 0x8000, -(b & 0x7FFF), b))
+        av = got[name].float().numpy()
+        bv = want[name].float().numpy()
+        flat_b = np.abs(bv).reshape(bv.shape[0], -1).max(axis=1)
+        tol = (2.0 ** -7 * flat_b).reshape((-1,) + (1,) * (bv.ndim - 1))
+        within = (ulp <= 2) | (np.abs(av - bv) <= tol)
+        exact_needed = name in ("embedding", "residual")
+        good = bool((ulp == 0).all()) if exact_needed else bool(within.all())
+        ok = ok and good
+        report[name] = {"worst_bf16_ulp": int(ulp.max()), "not_bit_exact": int((ulp > 0).sum()),
+                        "ok": good}
+    return {"rows_per_gpu": n, "gathered_from": world, "against": "svllm_ops CPU backend",
+            "ops": report, "ok": ok}
 
 
 # ---------------------------------------------------------------------------------------------

@@ -46,7 +46,7 @@ __device__ __forceinline__ int64_t load_id(const void* ids, int is_i64, int64_t 
                 : static_cast<int64_t>(__ldg(static_cast<const int*>(ids) + t));
 }
 
-__global__ void __launch_bounds__(256) embedding_bulk_kernel(const EmbArgs a) {
+__global__ void __launch_bounds__(512) embedding_bulk_kernel(const EmbArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warps = blockDim.x / kWarpSize;
   const int warp = threadIdx.x / kWarpSize;

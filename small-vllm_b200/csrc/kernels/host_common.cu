@@ -20,13 +20,16 @@ constexpr int kMaxDevices = 64;
 std::atomic<int> g_sm_count[kMaxDevices];
 std::atomic<int*> g_error_word[kMaxDevices];
 
+// Target bytes per stage, stages per warp, warps per CTA. Enough warps per SM to hide the
+// per-row latency chains, and (stages - 1) * unit bytes * warps of loads in flight per SM,
+// well above the ~45 KB that 6.5 TB/s over 148 SMs needs at ~1 us of memory latency.
 PipelineShape g_shapes[static_cast<int>(OpId::kCount)] = {
-    {8192, 4, 4},   // rms_norm
-    {8192, 4, 4},   // add_rms_norm
-    {8192, 4, 4},   // qk_norm_rope (a unit is one token; unit_bytes is unused)
-    {8192, 4, 4},   // rope
-    {8192, 4, 4},   // silu_and_mul
-    {8192, 4, 4},   // embedding
+    {4096, 3, 16},  // rms_norm
+    {4096, 3, 16},  // add_rms_norm
+    {4096, 3, 12},  // qk_norm_rope (a unit is one token; unit_bytes is unused)
+    {4096, 3, 12},  // rope
+    {4096, 3, 16},  // silu_and_mul
+    {4096, 4, 16},  // embedding (a unit is one row; unit_bytes is unused)
 };
 
 const char* const kOpNames[] = {"rms_norm", "add_rms_norm", "qk_norm_rope",

@@ -12,8 +12,19 @@
 //     straight to global memory, then lane 0 refills the stage. A row belongs to G lanes
 //     (G = 4..32, a power of two) that hold V 16-byte vectors each, so the sum of squares needs
 //     only log2(G) xor shuffles and no block barrier. The weight vector sits in shared memory.
-//   * Plain path, for rows that are not 16-byte aligned or not a multiple of 16 bytes: one
-//     warp per row, element loads, two passes (the second hits L1/L2). Still on the GPU.
+//   * Row-block path, for rows that are not 16-byte aligned, not a multiple of 16 bytes, or
+//     longer than the bulk path holds in registers: one CTA per row, two passes over the row
+//     (the second hits L1/L2). Still on the GPU.
+//
+// Summation order. For bf16 the sum of squares is accumulated in exactly the order of the
+// reference's CUDA kernel (rms_norm.cu:74-81 with block_sum, :31-56): thread t of a CTA of
+// B = min(1024, round_up(units, 32)) threads sums its 8-element vectors (or elements, when the
+// rows are not vectorisable) t, t + B, ... in order with fused multiply-adds; each warp reduces
+// by xor shuffles with offsets 16..1; the warp sums are then combined by one more 32-lane xor
+// tree in which the slots past the last warp hold zero; and the inverse RMS is
+// rsqrtf(sum / hidden + eps). The bulk path maps warp w, lane l of that CTA onto vector v = w of
+// lane l, keeps one partial per v, and replays the same tree, so the output is bit-identical to
+// the reference kernel's, not merely within a rounding step of it.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -60,7 +71,7 @@ __device__ __forceinline__ void load_rows(uint8_t* dst, const void* base, int64_
 }
 
 template <class E, int G, int V, bool kAdd>
-__global__ void __launch_bounds__(256) norm_bulk_kernel(const NormArgs a) {
+__global__ void __launch_bounds__(512) norm_bulk_kernel(const NormArgs a) {
   using S = typename E::Storage;
   constexpr int kVec = E::kPerVec;
   constexpr int kRowsPerPass = kWarpSize / G;
@@ -112,7 +123,7 @@ __global__ void __launch_bounds__(256) norm_bulk_kernel(const NormArgs a) {
     for (int64_t j = 0; j < min(static_cast<int64_t>(a.stages), n); ++j) issue(j);
   }
 
-  const float inv_hidden_div = static_cast<float>(hidden);
+  const float hidden_f = static_cast<float>(hidden);
   int64_t j = 0;
   for (; j < n; ++j) {
     const int s = static_cast<int>(j % a.stages);
@@ -128,10 +139,11 @@ __global__ void __launch_bounds__(256) norm_bulk_kernel(const NormArgs a) {
       const int rl = pass * kRowsPerPass + lane / G;  // row within the unit
       const uint8_t* xs = st + rl * row_bytes;
       uint4 hv[V];
-      float ss = 0.0f;
+      float part[V];
 #pragma unroll
       for (int v = 0; v < V; ++v) {
         const int c = sub + G * v;
+        part[v] = 0.0f;
         if (c < nvec) {
           uint4 raw = ld_shared_v4(xs + c * 16);
           if constexpr (kAdd) {
@@ -147,13 +159,27 @@ __global__ void __launch_bounds__(256) norm_bulk_kernel(const NormArgs a) {
           float f[kVec];
           unpack<E>(raw, f);
 #pragma unroll
-          for (int e = 0; e < kVec; ++e) ss = __fmaf_rn(f[e], f[e], ss);
+          for (int e = 0; e < kVec; ++e) part[v] = __fmaf_rn(f[e], f[e], part[v]);
         } else {
           hv[v] = make_uint4(0, 0, 0, 0);
         }
       }
-      ss = group_sum<G>(ss);
-      const float inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, inv_hidden_div), a.eps)));
+      float total;
+      if constexpr (V == 1) {
+        total = group_sum<G>(part[0]);
+      } else {
+        // vector v of every lane is warp v of the reference's CTA: reduce each, then combine
+        // the warp sums with the reference's final xor tree (slots past V hold zero)
+#pragma unroll
+        for (int v = 0; v < V; ++v) part[v] = group_sum<kWarpSize>(part[v]);
+#pragma unroll
+        for (int off = V / 2; off >= 1; off /= 2) {
+#pragma unroll
+          for (int i = 0; i < off; ++i) part[i] = __fadd_rn(part[i], part[i + off]);
+        }
+        total = part[0];
+      }
+      const float inv_rms = rsqrtf(__fadd_rn(__fdiv_rn(total, hidden_f), a.eps));
 
       if (rl < rows) {
         const int64_t row = r0 + rl;
@@ -194,37 +220,71 @@ __global__ void __launch_bounds__(256) norm_bulk_kernel(const NormArgs a) {
   }
 }
 
-// Plain-load path: one warp per row, grid-stride over rows.
-template <class E, bool kAdd>
-__global__ void __launch_bounds__(256) norm_plain_kernel(const NormArgs a) {
+// Row-block path: one CTA per row (grid-stride over rows), N elements per load (N = 8 for
+// 16-byte bf16 vectors, 4 for fp32, 1 when the rows are not vectorisable), the reference's
+// thread-to-element mapping and reduction tree.
+template <class E, int N, bool kAdd>
+__global__ void __launch_bounds__(1024) norm_rowblock_kernel(const NormArgs a) {
   using S = typename E::Storage;
+  struct alignas(sizeof(S) * N) Pack {
+    S v[N];
+  };
+  __shared__ float warp_sums[kWarpSize];
+  __shared__ float row_total;
+  const int units = a.hidden / N;
+  const int warp = threadIdx.x / kWarpSize;
   const int lane = threadIdx.x % kWarpSize;
-  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x / kWarpSize);
-  const int hidden = a.hidden;
-  const S* w = static_cast<const S*>(a.weight);
-  for (int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / kWarpSize) +
-                     threadIdx.x / kWarpSize;
-       row < a.num_rows; row += warps_total) {
-    const S* x = static_cast<const S*>(a.x) + row * a.x_stride;
-    S* out = static_cast<S*>(a.out) + row * a.out_stride;
-    S* res = kAdd ? static_cast<S*>(a.residual) + row * a.res_stride : nullptr;
-    float ss = 0.0f;
-    for (int i = lane; i < hidden; i += kWarpSize) {
-      float v = E::to_float(x[i]);
+  const int num_warps = blockDim.x / kWarpSize;
+  const Pack* w = static_cast<const Pack*>(a.weight);
+  const float hidden_f = static_cast<float>(a.hidden);
+
+  for (int64_t row = blockIdx.x; row < a.num_rows; row += gridDim.x) {
+    const Pack* x = reinterpret_cast<const Pack*>(static_cast<const S*>(a.x) + row * a.x_stride);
+    Pack* res = kAdd ? reinterpret_cast<Pack*>(static_cast<S*>(a.residual) + row * a.res_stride)
+                     : nullptr;
+    Pack* out = reinterpret_cast<Pack*>(static_cast<S*>(a.out) + row * a.out_stride);
+
+    float part = 0.0f;
+    for (int u = threadIdx.x; u < units; u += blockDim.x) {
+      Pack p = x[u];
       if constexpr (kAdd) {
-        v = E::round(__fadd_rn(v, E::to_float(res[i])));
-        res[i] = E::from_float(v);
+        const Pack r = res[u];
+#pragma unroll
+        for (int j = 0; j < N; ++j) {
+          p.v[j] = E::from_float(__fadd_rn(E::to_float(p.v[j]), E::to_float(r.v[j])));
+        }
+        res[u] = p;
       }
-      ss = __fmaf_rn(v, v, ss);
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        const float f = E::to_float(p.v[j]);
+        part = __fmaf_rn(f, f, part);
+      }
     }
-    ss = group_sum<kWarpSize>(ss);
-    const float inv_rms =
-        __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(hidden)), a.eps)));
-    for (int i = lane; i < hidden; i += kWarpSize) {
-      // Each lane re-reads only elements it read (and, for add, wrote) itself above.
-      const float v = kAdd ? E::to_float(res[i]) : E::to_float(x[i]);
-      out[i] = E::from_float(__fmul_rn(E::round(__fmul_rn(v, inv_rms)), E::to_float(w[i])));
+    part = group_sum<kWarpSize>(part);
+    if (lane == 0) warp_sums[warp] = part;
+    __syncthreads();
+    if (warp == 0) {
+      float v = lane < num_warps ? warp_sums[lane] : 0.0f;
+      v = group_sum<kWarpSize>(v);
+      if (lane == 0) row_total = v;
     }
+    __syncthreads();
+    const float inv_rms = rsqrtf(__fadd_rn(__fdiv_rn(row_total, hidden_f), a.eps));
+
+    // Each thread re-reads only the units it read (and, for add, wrote) in the first pass.
+    for (int u = threadIdx.x; u < units; u += blockDim.x) {
+      const Pack p = kAdd ? res[u] : x[u];
+      const Pack wv = w[u];
+      Pack o;
+#pragma unroll
+      for (int j = 0; j < N; ++j) {
+        const float n = E::round(__fmul_rn(E::to_float(p.v[j]), inv_rms));
+        o.v[j] = E::from_float(__fmul_rn(n, E::to_float(wv.v[j])));
+      }
+      out[u] = o;
+    }
+    __syncthreads();  // warp_sums and row_total are reused by the next row
   }
 }
 
@@ -322,9 +382,18 @@ int launch_norm(void* out, const void* x, void* residual, const void* weight, in
     }
   }
 
-  constexpr int kThreads = 256;
-  const int64_t grid = persistent_grid((num_rows + 7) / 8, device, 8);
-  norm_plain_kernel<E, kAdd><<<static_cast<unsigned>(grid), kThreads, 0, stream>>>(a);
+  // Row-block path, vectorised exactly when the reference's kernel is (rms_norm.cu:122-127):
+  // a row length that is a multiple of the vector and 16-byte aligned base pointers.
+  constexpr int kVec = E::kPerVec;
+  const bool vec = hidden % kVec == 0 && aligned16(out) && aligned16(x) && aligned16(weight) &&
+                   (!kAdd || aligned16(residual)) && out_stride % kVec == 0 &&
+                   x_stride % kVec == 0 && (!kAdd || res_stride % kVec == 0);
+  const int64_t units = vec ? hidden / kVec : hidden;
+  const int threads = static_cast<int>(std::min<int64_t>(1024, round_up(units, kWarpSize)));
+  const auto kernel = vec ? norm_rowblock_kernel<E, kVec, kAdd> : norm_rowblock_kernel<E, 1, kAdd>;
+  const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(kernel), threads, 0, device);
+  const int64_t grid = persistent_grid(num_rows, device, per_sm > 0 ? per_sm : 1);
+  kernel<<<static_cast<unsigned>(grid), threads, 0, stream>>>(a);
   return launch_status();
 }
 

@@ -48,6 +48,7 @@ struct RopeArgs {
   int num_kv_heads;
   int head_dim;
   int pos_is_i64;
+  int norm_vec;  // plain path: the reference would load 8-element vectors
   float eps;
   int* err;
   // bulk-copy path
@@ -80,7 +81,7 @@ __device__ __forceinline__ void rotate(float (&lo)[E::kPerVec], float (&hi)[E::k
 }
 
 template <class E, int G, bool kNorm>
-__global__ void __launch_bounds__(256) rope_bulk_kernel(const __grid_constant__ RopeArgs a) {
+__global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ RopeArgs a) {
   using S = typename E::Storage;
   constexpr int kVec = E::kPerVec;
   constexpr int kHalf = kVec * G;  // head_dim / 2
@@ -180,15 +181,23 @@ __global__ void __launch_bounds__(256) rope_bulk_kernel(const __grid_constant__ 
       unpack<E>(ld_shared_v4(hs + kHalf * sizeof(S) + sub * 16), hi);
       const bool is_q = h < num_heads;
       if constexpr (kNorm) {
-        float ss = 0.0f;
+        // The head's sum of squares in the order of the reference's rms_norm kernel run on the
+        // [tokens * heads, head_dim] view: lane j holds that kernel's vectors j (lo) and j + G
+        // (hi); its xor tree first adds vector j + G to vector j (offset G), then reduces over
+        // the G lanes; at head_dim 512 the two halves are two warps whose sums are added last.
+        float p_lo = 0.0f, p_hi = 0.0f;
 #pragma unroll
         for (int e = 0; e < kVec; ++e) {
-          ss = __fmaf_rn(lo[e], lo[e], ss);
-          ss = __fmaf_rn(hi[e], hi[e], ss);
+          p_lo = __fmaf_rn(lo[e], lo[e], p_lo);
+          p_hi = __fmaf_rn(hi[e], hi[e], p_hi);
         }
-        ss = group_sum<G>(ss);
-        const float inv_rms = __fdiv_rn(
-            1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(kDim)), a.eps)));
+        float total;
+        if constexpr (2 * G <= kWarpSize) {
+          total = group_sum<G>(__fadd_rn(p_lo, p_hi));
+        } else {
+          total = __fadd_rn(group_sum<G>(p_lo), group_sum<G>(p_hi));
+        }
+        const float inv_rms = rsqrtf(__fadd_rn(__fdiv_rn(total, static_cast<float>(kDim)), a.eps));
 #pragma unroll
         for (int e = 0; e < kVec; ++e) {
           lo[e] = E::round(__fmul_rn(E::round(__fmul_rn(lo[e], inv_rms)), is_q ? qw_lo[e] : kw_lo[e]));
@@ -222,6 +231,35 @@ __global__ void __launch_bounds__(256) rope_bulk_kernel(const __grid_constant__ 
   }
 }
 
+// 1 / RMS of one head of n values, summed by one warp in the order of the reference's rms_norm
+// kernel on that row: a CTA of round_up(units, 32) threads, thread t summing unit t (an 8-element
+// vector when vec, else one element), per-warp xor trees, then a final 32-slot xor tree over the
+// warp sums with zeros past the last warp. Lane l plays thread l + 32 w of every warp w.
+template <class E>
+__device__ float reference_order_inv_rms(const typename E::Storage* x, int n, float eps, int vec,
+                                         int lane) {
+  constexpr int kMaxWarps = 32;
+  const int per = vec ? 8 : 1;
+  const int units = n / per;
+  const int num_warps = (units + kWarpSize - 1) / kWarpSize;
+  float slots[kMaxWarps];
+  for (int w = 0; w < kMaxWarps; ++w) {
+    float p = 0.0f;
+    const int u = w * kWarpSize + lane;
+    if (w < num_warps && u < units) {
+      for (int j = 0; j < per; ++j) {
+        const float f = E::to_float(x[u * per + j]);
+        p = __fmaf_rn(f, f, p);
+      }
+    }
+    slots[w] = w < num_warps ? group_sum<kWarpSize>(p) : 0.0f;
+  }
+  for (int off = kMaxWarps / 2; off >= 1; off /= 2) {
+    for (int i = 0; i < off; ++i) slots[i] = __fadd_rn(slots[i], slots[i + off]);
+  }
+  return rsqrtf(__fadd_rn(__fdiv_rn(slots[0], static_cast<float>(n)), eps));
+}
+
 // Plain path: one warp per token, any head_dim (even), any alignment.
 template <class E, bool kNorm>
 __global__ void __launch_bounds__(256) rope_plain_kernel(const __grid_constant__ RopeArgs a) {
@@ -243,13 +281,7 @@ __global__ void __launch_bounds__(256) rope_plain_kernel(const __grid_constant__
                   : static_cast<S*>(a.k) + t * a.k_stride + static_cast<int64_t>(h - a.num_heads) * dim;
       float inv_rms = 1.0f;
       if constexpr (kNorm) {
-        float ss = 0.0f;
-        for (int i = lane; i < dim; i += kWarpSize) {
-          const float v = E::to_float(x[i]);
-          ss = __fmaf_rn(v, v, ss);
-        }
-        ss = group_sum<kWarpSize>(ss);
-        inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(dim)), a.eps)));
+        inv_rms = reference_order_inv_rms<E>(x, dim, a.eps, a.norm_vec, lane);
       }
       __syncwarp();
       for (int i = lane; i < half; i += kWarpSize) {
@@ -334,6 +366,9 @@ int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
   a.eps = eps;
   a.err = err;
   std::memcpy(a.inv_freq, inv_freq, sizeof(float) * (head_dim / 2));
+  a.norm_vec = sizeof(S) == 2 && head_dim % 8 == 0 && aligned16(q) && aligned16(k) &&
+               (q_stride * sizeof(S)) % 16 == 0 && (k_stride * sizeof(S)) % 16 == 0 &&
+               (!kNorm || (aligned16(a.q_weight) && aligned16(a.k_weight)));
 
   const int64_t head_bytes = head_dim * static_cast<int64_t>(sizeof(S));
   const int64_t q_bytes = num_heads * head_bytes;

@@ -45,7 +45,7 @@ __device__ __forceinline__ float silu(float g) {
 }
 
 template <class E>
-__global__ void __launch_bounds__(256) silu_bulk_kernel(const SiluArgs a) {
+__global__ void __launch_bounds__(512) silu_bulk_kernel(const SiluArgs a) {
   using S = typename E::Storage;
   constexpr int kVec = E::kPerVec;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -104,6 +104,7 @@ __global__ void __launch_bounds__(256) silu_bulk_kernel(const SiluArgs a) {
     unit_of(u0 + j, row, col, len);
     S* out = static_cast<S*>(a.out) + row * a.out_stride + col;
     const int nv = len / kVec;
+#pragma unroll 2
     for (int v = lane; v < nv; v += kWarpSize) {
       float g[kVec], u[kVec];
       unpack<E>(ld_shared_v4(st + v * 16), g);

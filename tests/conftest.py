@@ -115,13 +115,16 @@ def assert_bf16_within_ulp(actual, expected, max_ulp: int, what: str = "") -> fl
     return float((d == 0).mean())
 
 
-def assert_rel_f32(actual, expected, rtol: float = 1e-5, what: str = "") -> None:
-    """fp32: |a - e| <= rtol * |e| per element (the oracle bar for fp32 outputs), with an
-    absolute floor of rtol * (largest |e| in the row) for values that cancel to near zero."""
+def assert_rel_f32(actual, expected, rtol: float = 1e-5, what: str = "", scale=None) -> None:
+    """fp32: |a - e| <= rtol * max(|e|, s) per element (the north star's 1e-5 relative bar),
+    where s is the magnitude the element was computed from: by default the RMS of its row (the
+    last axis), so a value that cancels to near zero is held to the row's scale, not its own."""
     a = np.asarray(to_bits(actual), dtype=np.float64)
     e = np.asarray(to_bits(expected), dtype=np.float64)
-    floor = rtol * np.abs(e).max(axis=-1, keepdims=True) if e.ndim else 0.0
-    bad = np.abs(a - e) > rtol * np.abs(e) + floor * 1e-2
+    if scale is None:
+        scale = np.sqrt((e ** 2).mean(axis=-1, keepdims=True)) if e.ndim else np.abs(e)
+    bound = rtol * np.maximum(np.abs(e), scale)
+    bad = np.abs(a - e) > bound
     assert not bad.any(), (f"{what}: {int(bad.sum())} of {bad.size} fp32 elements off by more "
                            f"than {rtol} relative (worst {np.abs(a - e)[bad].max()})")
 
