@@ -90,6 +90,96 @@ __device__ __forceinline__ uint4 pack<F32>(const float (&f)[4]) {
 }
 
 // ---------------------------------------------------------------------------------------------
+// Packed bf16 arithmetic. For bf16 operands these give exactly the result of the fp32 operation
+// followed by one round-to-nearest-even to bf16 (the sequence a bf16 torch op performs):
+//   * the product of two bf16 values has a 16-bit significand, so it is exact in fp32 and the
+//     fp32 rounding step is the identity;
+//   * a sum or difference is exact in fp32 unless the exponents differ by 16 or more, and then
+//     the smaller operand is below 2^-8 of the larger's last bf16 place, so both routes round to
+//     the larger operand.
+// (Both arguments assume normal numbers; bf16 subnormals, below 1.2e-38, never occur in these
+// ops' activations.) One instruction handles two elements.
+
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// Two fp32 values rounded to nearest even into one bf16x2 word (lo in the low half).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t word(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Per-vector steps shared by the norm kernels.
+
+// residual' = round(x + residual) for one 16-byte vector.
+template <class E>
+__device__ __forceinline__ uint4 add_vec(const uint4& x, const uint4& r);
+
+template <>
+__device__ __forceinline__ uint4 add_vec<Bf16>(const uint4& x, const uint4& r) {
+  return make_uint4(bf16x2_add(x.x, r.x), bf16x2_add(x.y, r.y), bf16x2_add(x.z, r.z),
+                    bf16x2_add(x.w, r.w));
+}
+
+template <>
+__device__ __forceinline__ uint4 add_vec<F32>(const uint4& x, const uint4& r) {
+  return make_uint4(__float_as_uint(__fadd_rn(__uint_as_float(x.x), __uint_as_float(r.x))),
+                    __float_as_uint(__fadd_rn(__uint_as_float(x.y), __uint_as_float(r.y))),
+                    __float_as_uint(__fadd_rn(__uint_as_float(x.z), __uint_as_float(r.z))),
+                    __float_as_uint(__fadd_rn(__uint_as_float(x.w), __uint_as_float(r.w))));
+}
+
+// out = round(round(h * inv_rms) * w) for one 16-byte vector of h and of the weight.
+template <class E>
+__device__ __forceinline__ uint4 normalize_vec(const uint4& h, float inv_rms, const uint4& w);
+
+template <>
+__device__ __forceinline__ uint4 normalize_vec<Bf16>(const uint4& h, float inv_rms,
+                                                     const uint4& w) {
+  float f[8];
+  unpack<Bf16>(h, f);
+  uint32_t n[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    n[i] = pack_bf16x2(__fmul_rn(f[2 * i], inv_rms), __fmul_rn(f[2 * i + 1], inv_rms));
+  }
+  return make_uint4(bf16x2_mul(n[0], w.x), bf16x2_mul(n[1], w.y), bf16x2_mul(n[2], w.z),
+                    bf16x2_mul(n[3], w.w));
+}
+
+template <>
+__device__ __forceinline__ uint4 normalize_vec<F32>(const uint4& h, float inv_rms,
+                                                    const uint4& w) {
+  float f[4], wf[4];
+  unpack<F32>(h, f);
+  unpack<F32>(w, wf);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) f[e] = __fmul_rn(__fmul_rn(f[e], inv_rms), wf[e]);
+  return pack<F32>(f);
+}
+
+// ---------------------------------------------------------------------------------------------
 // Global memory access with streaming hints.
 
 __device__ __forceinline__ uint4 ld_global_nc_v4(const void* p) {

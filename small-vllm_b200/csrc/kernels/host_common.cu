@@ -20,16 +20,19 @@ constexpr int kMaxDevices = 64;
 std::atomic<int> g_sm_count[kMaxDevices];
 std::atomic<int*> g_error_word[kMaxDevices];
 
-// Target bytes per stage, stages per warp, warps per CTA. Enough warps per SM to hide the
-// per-row latency chains, and (stages - 1) * unit bytes * warps of loads in flight per SM,
-// well above the ~45 KB that 6.5 TB/s over 148 SMs needs at ~1 us of memory latency.
+// Target bytes per stage, stages per warp, warps per CTA (the occupancy calculator then packs
+// as many CTAs per SM as shared memory and registers allow). Chosen by sweeping each op on a
+// B200 at 1M tokens of the Qwen3-0.6B shapes: the streaming ops want (stages - 1) * unit bytes *
+// resident warps of loads in flight per SM well above the ~45 KB that 6.5 TB/s over 148 SMs
+// needs at ~1 us of memory latency; the compute-heavier ops (SiLU, q/k norm + RoPE) also want
+// many resident warps to hide their latency chains.
 PipelineShape g_shapes[static_cast<int>(OpId::kCount)] = {
-    {4096, 3, 16},  // rms_norm
-    {4096, 3, 16},  // add_rms_norm
-    {4096, 3, 12},  // qk_norm_rope (a unit is one token; unit_bytes is unused)
-    {4096, 3, 12},  // rope
-    {4096, 3, 16},  // silu_and_mul
-    {4096, 4, 16},  // embedding (a unit is one row; unit_bytes is unused)
+    {8192, 2, 12},  // rms_norm
+    {8192, 3, 8},   // add_rms_norm
+    {4096, 2, 16},  // qk_norm_rope (a unit is one token; unit_bytes is unused)
+    {4096, 2, 16},  // rope
+    {4096, 2, 12},  // silu_and_mul
+    {4096, 2, 16},  // embedding (a unit is one row; unit_bytes is unused)
 };
 
 const char* const kOpNames[] = {"rms_norm", "add_rms_norm", "qk_norm_rope",

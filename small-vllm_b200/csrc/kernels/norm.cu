@@ -147,13 +147,7 @@ __global__ void __launch_bounds__(512) norm_bulk_kernel(const NormArgs a) {
         if (c < nvec) {
           uint4 raw = ld_shared_v4(xs + c * 16);
           if constexpr (kAdd) {
-            const uint4 rr = ld_shared_v4(xs + a.rows_per_unit * row_bytes + c * 16);
-            float xf[kVec], rf[kVec];
-            unpack<E>(raw, xf);
-            unpack<E>(rr, rf);
-#pragma unroll
-            for (int e = 0; e < kVec; ++e) xf[e] = __fadd_rn(xf[e], rf[e]);
-            raw = pack<E>(xf);  // residual + x, rounded to the storage type
+            raw = add_vec<E>(raw, ld_shared_v4(xs + a.rows_per_unit * row_bytes + c * 16));
           }
           hv[v] = raw;
           float f[kVec];
@@ -190,12 +184,8 @@ __global__ void __launch_bounds__(512) norm_bulk_kernel(const NormArgs a) {
           const int c = sub + G * v;
           if (c < nvec) {
             if constexpr (kAdd) st_global_v4(res_row + c * kVec, hv[v]);
-            float f[kVec], w[kVec];
-            unpack<E>(hv[v], f);
-            unpack<E>(ld_shared_v4(wsm + c * 16), w);
-#pragma unroll
-            for (int e = 0; e < kVec; ++e) f[e] = __fmul_rn(E::round(__fmul_rn(f[e], inv_rms)), w[e]);
-            st_global_v4(out_row + c * kVec, pack<E>(f));
+            st_global_v4(out_row + c * kVec,
+                         normalize_vec<E>(hv[v], inv_rms, ld_shared_v4(wsm + c * 16)));
           }
         }
       }

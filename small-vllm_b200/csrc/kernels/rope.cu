@@ -66,9 +66,10 @@ __device__ __forceinline__ float load_position(const void* positions, int is_i64
   return __int2float_rn(__ldg(static_cast<const int*>(positions) + t));
 }
 
-// Rotation of one lane's pair block: lo[e] = x[i], hi[e] = x[i + d/2] for kVec consecutive i.
+// Rotation of one lane's pair block: lo[e] = x[i], hi[e] = x[i + d/2] for kVec consecutive i,
+// in fp32 with the storage type's rounding after every step.
 template <class E>
-__device__ __forceinline__ void rotate(float (&lo)[E::kPerVec], float (&hi)[E::kPerVec],
+__device__ __forceinline__ void rotate_pairs(float (&lo)[E::kPerVec], float (&hi)[E::kPerVec],
                                        const float (&c)[E::kPerVec],
                                        const float (&s)[E::kPerVec]) {
 #pragma unroll
@@ -79,6 +80,55 @@ __device__ __forceinline__ void rotate(float (&lo)[E::kPerVec], float (&hi)[E::k
     hi[e] = __fadd_rn(E::round(__fmul_rn(x2, c[e])), E::round(__fmul_rn(x1, s[e])));
   }
 }
+
+// cos and sin of one lane's kVec rotation pairs, rounded to the storage type (Hugging Face's
+// rotary embedding returns them in the activation dtype), kept packed for bf16.
+template <class E>
+struct LaneTrig;
+
+template <>
+struct LaneTrig<Bf16> {
+  uint32_t c[4], s[4];
+  __device__ __forceinline__ void load(const float* cs, const float* sn) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      c[i] = pack_bf16x2(cs[2 * i], cs[2 * i + 1]);
+      s[i] = pack_bf16x2(sn[2 * i], sn[2 * i + 1]);
+    }
+  }
+  // lo = x[i], hi = x[i + d/2]: lo' = round(lo*c) - round(hi*s), hi' = round(hi*c) + round(lo*s)
+  __device__ __forceinline__ void rotate(uint4& lo, uint4& hi) const {
+    uint32_t l[4], h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t wl = word(lo, i), wh = word(hi, i);
+      l[i] = bf16x2_sub(bf16x2_mul(wl, c[i]), bf16x2_mul(wh, s[i]));
+      h[i] = bf16x2_add(bf16x2_mul(wh, c[i]), bf16x2_mul(wl, s[i]));
+    }
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+  }
+};
+
+template <>
+struct LaneTrig<F32> {
+  float c[4], s[4];
+  __device__ __forceinline__ void load(const float* cs, const float* sn) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      c[i] = cs[i];
+      s[i] = sn[i];
+    }
+  }
+  __device__ __forceinline__ void rotate(uint4& lo, uint4& hi) const {
+    float l[4], h[4];
+    unpack<F32>(lo, l);
+    unpack<F32>(hi, h);
+    rotate_pairs<F32>(l, h, c, s);
+    lo = pack<F32>(l);
+    hi = pack<F32>(h);
+  }
+};
 
 template <class E, int G, bool kNorm>
 __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ RopeArgs a) {
@@ -111,14 +161,14 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
   }
 
   // Per-lane norm weights: this lane's block of each half of q_weight and k_weight.
-  float qw_lo[kVec], qw_hi[kVec], kw_lo[kVec], kw_hi[kVec];
+  uint4 qw_lo{}, qw_hi{}, kw_lo{}, kw_hi{};
   if constexpr (kNorm) {
     const uint8_t* qw = static_cast<const uint8_t*>(a.q_weight);
     const uint8_t* kw = static_cast<const uint8_t*>(a.k_weight);
-    unpack<E>(ld_global_nc_v4(qw + sub * 16), qw_lo);
-    unpack<E>(ld_global_nc_v4(qw + (kHalf * sizeof(S)) + sub * 16), qw_hi);
-    unpack<E>(ld_global_nc_v4(kw + sub * 16), kw_lo);
-    unpack<E>(ld_global_nc_v4(kw + (kHalf * sizeof(S)) + sub * 16), kw_hi);
+    qw_lo = ld_global_nc_v4(qw + sub * 16);
+    qw_hi = ld_global_nc_v4(qw + (kHalf * sizeof(S)) + sub * 16);
+    kw_lo = ld_global_nc_v4(kw + sub * 16);
+    kw_hi = ld_global_nc_v4(kw + (kHalf * sizeof(S)) + sub * 16);
   }
   __syncthreads();
 
@@ -159,12 +209,8 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
       sin_sm[i] = sinf(angle);
     }
     __syncwarp();
-    float c[kVec], s[kVec];
-#pragma unroll
-    for (int e = 0; e < kVec; ++e) {
-      c[e] = E::round(cos_sm[sub * kVec + e]);
-      s[e] = E::round(sin_sm[sub * kVec + e]);
-    }
+    LaneTrig<E> trig;
+    trig.load(cos_sm + sub * kVec, sin_sm + sub * kVec);
 
     const int stage = static_cast<int>(j % a.stages);
     const uint32_t parity = static_cast<uint32_t>((j / a.stages) & 1);
@@ -176,20 +222,22 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
       const int h = h0 + lane / G;
       const bool valid = h < total_heads;
       const uint8_t* hs = st + static_cast<size_t>(valid ? h : 0) * kDim * sizeof(S);
-      float lo[kVec], hi[kVec];
-      unpack<E>(ld_shared_v4(hs + sub * 16), lo);
-      unpack<E>(ld_shared_v4(hs + kHalf * sizeof(S) + sub * 16), hi);
+      uint4 lo = ld_shared_v4(hs + sub * 16);
+      uint4 hi = ld_shared_v4(hs + kHalf * sizeof(S) + sub * 16);
       const bool is_q = h < num_heads;
       if constexpr (kNorm) {
         // The head's sum of squares in the order of the reference's rms_norm kernel run on the
         // [tokens * heads, head_dim] view: lane j holds that kernel's vectors j (lo) and j + G
         // (hi); its xor tree first adds vector j + G to vector j (offset G), then reduces over
         // the G lanes; at head_dim 512 the two halves are two warps whose sums are added last.
+        float lf[kVec], hf[kVec];
+        unpack<E>(lo, lf);
+        unpack<E>(hi, hf);
         float p_lo = 0.0f, p_hi = 0.0f;
 #pragma unroll
         for (int e = 0; e < kVec; ++e) {
-          p_lo = __fmaf_rn(lo[e], lo[e], p_lo);
-          p_hi = __fmaf_rn(hi[e], hi[e], p_hi);
+          p_lo = __fmaf_rn(lf[e], lf[e], p_lo);
+          p_hi = __fmaf_rn(hf[e], hf[e], p_hi);
         }
         float total;
         if constexpr (2 * G <= kWarpSize) {
@@ -198,19 +246,16 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
           total = __fadd_rn(group_sum<G>(p_lo), group_sum<G>(p_hi));
         }
         const float inv_rms = rsqrtf(__fadd_rn(__fdiv_rn(total, static_cast<float>(kDim)), a.eps));
-#pragma unroll
-        for (int e = 0; e < kVec; ++e) {
-          lo[e] = E::round(__fmul_rn(E::round(__fmul_rn(lo[e], inv_rms)), is_q ? qw_lo[e] : kw_lo[e]));
-          hi[e] = E::round(__fmul_rn(E::round(__fmul_rn(hi[e], inv_rms)), is_q ? qw_hi[e] : kw_hi[e]));
-        }
+        lo = normalize_vec<E>(lo, inv_rms, is_q ? qw_lo : kw_lo);
+        hi = normalize_vec<E>(hi, inv_rms, is_q ? qw_hi : kw_hi);
       }
-      rotate<E>(lo, hi, c, s);
+      trig.rotate(lo, hi);
       if (valid) {
         S* dst = is_q ? static_cast<S*>(a.q) + t * a.q_stride + static_cast<int64_t>(h) * kDim
                       : static_cast<S*>(a.k) + t * a.k_stride +
                             static_cast<int64_t>(h - num_heads) * kDim;
-        st_global_v4(dst + sub * kVec, pack<E>(lo));
-        st_global_v4(dst + kHalf + sub * kVec, pack<E>(hi));
+        st_global_v4(dst + sub * kVec, lo);
+        st_global_v4(dst + kHalf + sub * kVec, hi);
       }
     }
     __syncwarp();
@@ -296,7 +341,7 @@ __global__ void __launch_bounds__(256) rope_plain_kernel(const __grid_constant__
         const float angle = __fmul_rn(pos, a.inv_freq[i]);
         c[0] = E::round(cosf(angle));
         s[0] = E::round(sinf(angle));
-        rotate<E>(lo, hi, c, s);
+        rotate_pairs<E>(lo, hi, c, s);
         x[i] = E::from_float(lo[0]);
         x[i + half] = E::from_float(hi[0]);
       }

@@ -44,6 +44,31 @@ __device__ __forceinline__ float silu(float g) {
   return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
 }
 
+// out = round(round(silu(g)) * u) for one 16-byte vector of gate and of up.
+template <class E>
+__device__ __forceinline__ uint4 silu_mul_vec(const uint4& g, const uint4& u);
+
+template <>
+__device__ __forceinline__ uint4 silu_mul_vec<Bf16>(const uint4& g, const uint4& u) {
+  float f[8];
+  unpack<Bf16>(g, f);
+  uint32_t s[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) s[i] = pack_bf16x2(silu(f[2 * i]), silu(f[2 * i + 1]));
+  return make_uint4(bf16x2_mul(s[0], u.x), bf16x2_mul(s[1], u.y), bf16x2_mul(s[2], u.z),
+                    bf16x2_mul(s[3], u.w));
+}
+
+template <>
+__device__ __forceinline__ uint4 silu_mul_vec<F32>(const uint4& g, const uint4& u) {
+  float f[4], uf[4];
+  unpack<F32>(g, f);
+  unpack<F32>(u, uf);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) f[e] = __fmul_rn(silu(f[e]), uf[e]);
+  return pack<F32>(f);
+}
+
 template <class E>
 __global__ void __launch_bounds__(512) silu_bulk_kernel(const SiluArgs a) {
   using S = typename E::Storage;
@@ -106,12 +131,8 @@ __global__ void __launch_bounds__(512) silu_bulk_kernel(const SiluArgs a) {
     const int nv = len / kVec;
 #pragma unroll 2
     for (int v = lane; v < nv; v += kWarpSize) {
-      float g[kVec], u[kVec];
-      unpack<E>(ld_shared_v4(st + v * 16), g);
-      unpack<E>(ld_shared_v4(st + half_stage + v * 16), u);
-#pragma unroll
-      for (int e = 0; e < kVec; ++e) g[e] = __fmul_rn(E::round(silu(g[e])), u[e]);
-      st_global_v4(out + v * kVec, pack<E>(g));
+      st_global_v4(out + v * kVec, silu_mul_vec<E>(ld_shared_v4(st + v * 16),
+                                                   ld_shared_v4(st + half_stage + v * 16)));
     }
     __syncwarp();
     if (lane == 0 && j + a.stages < n) {
