@@ -324,6 +324,16 @@ __device__ __forceinline__ float group_sum(float v) {
   return v;
 }
 
+// The units a warp processes: a contiguous, balanced share of n units (interleave = false), or
+// every warps_total-th unit starting at the warp's index (interleave = true), so that at any
+// moment the grid streams through neighbouring units of memory together.
+struct WarpUnits {
+  int64_t first;
+  int64_t step;
+  int64_t count;
+  __device__ __forceinline__ int64_t at(int64_t j) const { return first + j * step; }
+};
+
 // Balanced contiguous partition of n units over `parts` workers: worker i gets [begin, end).
 __device__ __forceinline__ void partition(int64_t n, int64_t parts, int64_t i, int64_t& begin,
                                           int64_t& end) {
@@ -331,6 +341,16 @@ __device__ __forceinline__ void partition(int64_t n, int64_t parts, int64_t i, i
   const int64_t rem = n % parts;
   begin = i * base + (i < rem ? i : rem);
   end = begin + base + (i < rem ? 1 : 0);
+}
+
+__device__ __forceinline__ WarpUnits warp_units(int64_t n, int64_t warps_total, int64_t gw,
+                                                bool interleave) {
+  if (interleave) {
+    return {gw, warps_total, gw < n ? (n - gw + warps_total - 1) / warps_total : 0};
+  }
+  int64_t begin, end;
+  partition(n, warps_total, gw, begin, end);
+  return {begin, 1, end - begin};
 }
 
 }  // namespace svllm::k

@@ -2,6 +2,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -127,6 +128,14 @@ int blocks_per_sm(const void* func, int threads, size_t smem_bytes, int device) 
   }
   if (g_occ_used < kOccCacheSize) g_occ[g_occ_used++] = {func, threads, smem_bytes, device, blocks};
   return blocks;
+}
+
+bool interleave_units() {
+  static const bool on = [] {
+    const char* v = std::getenv("SVLLM_INTERLEAVE");
+    return v != nullptr && v[0] == '1';
+  }();
+  return on;
 }
 
 int* library_error_word(int device) {

@@ -50,6 +50,8 @@ struct NormArgs {
   int* err;
   // bulk-copy path
   int rows_per_unit;     // R
+  int interleave;        // unit order (WarpUnits)
+  float inv_hidden;      // 1 / hidden when hidden is a power of two, else 0
   int stages;
   int stage_bytes;       // bytes of one stage (x rows, then residual rows)
   int weight_offset;     // byte offsets into dynamic shared memory
@@ -98,17 +100,16 @@ __global__ void __launch_bounds__(512) norm_bulk_kernel(const NormArgs a) {
   __syncthreads();
 
   const int64_t num_units = (a.num_rows + a.rows_per_unit - 1) / a.rows_per_unit;
-  int64_t u0, u1;
-  partition(num_units, static_cast<int64_t>(gridDim.x) * warps,
-            static_cast<int64_t>(blockIdx.x) * warps + warp, u0, u1);
-  const int64_t n = u1 - u0;
+  const WarpUnits wu = warp_units(num_units, static_cast<int64_t>(gridDim.x) * warps,
+                                  static_cast<int64_t>(blockIdx.x) * warps + warp, a.interleave);
+  const int64_t n = wu.count;
   const int64_t x_stride_b = a.x_stride * static_cast<int64_t>(sizeof(S));
   const int64_t r_stride_b = a.res_stride * static_cast<int64_t>(sizeof(S));
 
   auto issue = [&](int64_t j) {
     const int s = static_cast<int>(j % a.stages);
     uint8_t* st = ring + static_cast<size_t>(s) * a.stage_bytes;
-    const int64_t r0 = (u0 + j) * a.rows_per_unit;
+    const int64_t r0 = wu.at(j) * a.rows_per_unit;
     const int rows = static_cast<int>(min(static_cast<int64_t>(a.rows_per_unit), a.num_rows - r0));
     const uint32_t bytes = rows * row_bytes;
     mbar_arrive_expect_tx(&bars[s], kAdd ? 2 * bytes : bytes);
@@ -131,7 +132,7 @@ __global__ void __launch_bounds__(512) norm_bulk_kernel(const NormArgs a) {
     if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[s], parity))) break;
 
     const uint8_t* st = ring + static_cast<size_t>(s) * a.stage_bytes;
-    const int64_t r0 = (u0 + j) * a.rows_per_unit;
+    const int64_t r0 = wu.at(j) * a.rows_per_unit;
     const int rows = static_cast<int>(min(static_cast<int64_t>(a.rows_per_unit), a.num_rows - r0));
     const int sub = lane % G;
 
@@ -173,7 +174,10 @@ __global__ void __launch_bounds__(512) norm_bulk_kernel(const NormArgs a) {
         }
         total = part[0];
       }
-      const float inv_rms = rsqrtf(__fadd_rn(__fdiv_rn(total, hidden_f), a.eps));
+      // sum / hidden; a power-of-two hidden divides exactly as a multiply by its reciprocal
+      const float mean = a.inv_hidden != 0.0f ? __fmul_rn(total, a.inv_hidden)
+                                              : __fdiv_rn(total, hidden_f);
+      const float inv_rms = rsqrtf(__fadd_rn(mean, a.eps));
 
       if (rl < rows) {
         const int64_t row = r0 + rl;
@@ -260,7 +264,9 @@ __global__ void __launch_bounds__(1024) norm_rowblock_kernel(const NormArgs a) {
       if (lane == 0) row_total = v;
     }
     __syncthreads();
-    const float inv_rms = rsqrtf(__fadd_rn(__fdiv_rn(row_total, hidden_f), a.eps));
+    const float mean = a.inv_hidden != 0.0f ? __fmul_rn(row_total, a.inv_hidden)
+                                            : __fdiv_rn(row_total, hidden_f);
+    const float inv_rms = rsqrtf(__fadd_rn(mean, a.eps));
 
     // Each thread re-reads only the units it read (and, for add, wrote) in the first pass.
     for (int u = threadIdx.x; u < units; u += blockDim.x) {
@@ -328,6 +334,8 @@ int launch_norm(void* out, const void* x, void* residual, const void* weight, in
   a.hidden = static_cast<int>(hidden);
   a.eps = eps;
   a.err = err;
+  a.interleave = interleave_units() ? 1 : 0;
+  a.inv_hidden = (hidden & (hidden - 1)) == 0 ? 1.0f / static_cast<float>(hidden) : 0.0f;
 
   const int64_t row_bytes = hidden * static_cast<int64_t>(sizeof(S));
   const bool bulk_ok = aligned16(out) && aligned16(x) && aligned16(weight) &&

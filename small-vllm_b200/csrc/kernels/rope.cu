@@ -49,6 +49,7 @@ struct RopeArgs {
   int head_dim;
   int pos_is_i64;
   int norm_vec;  // plain path: the reference would load 8-element vectors
+  int interleave;  // token order (WarpUnits)
   float eps;
   int* err;
   // bulk-copy path
@@ -172,17 +173,16 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
   }
   __syncthreads();
 
-  int64_t t0, t1;
-  partition(a.num_tokens, static_cast<int64_t>(gridDim.x) * warps,
-            static_cast<int64_t>(blockIdx.x) * warps + warp, t0, t1);
-  const int64_t n = t1 - t0;
+  const WarpUnits wu = warp_units(a.num_tokens, static_cast<int64_t>(gridDim.x) * warps,
+                                  static_cast<int64_t>(blockIdx.x) * warps + warp, a.interleave);
+  const int64_t n = wu.count;
   const int64_t q_stride_b = a.q_stride * static_cast<int64_t>(sizeof(S));
   const int64_t k_stride_b = a.k_stride * static_cast<int64_t>(sizeof(S));
 
   auto issue = [&](int64_t j) {
     const int s = static_cast<int>(j % a.stages);
     uint8_t* st = ring + static_cast<size_t>(s) * a.stage_bytes;
-    const int64_t t = t0 + j;
+    const int64_t t = wu.at(j);
     mbar_arrive_expect_tx(&bars[s], q_bytes + k_bytes);
     if (q_bytes) bulk_load(st, static_cast<const uint8_t*>(a.q) + t * q_stride_b, q_bytes, &bars[s]);
     if (k_bytes) {
@@ -195,18 +195,17 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
   }
 
   // Positions run one token ahead of use, so their load latency hides behind a token's work.
-  float pos_next = n > 0 ? load_position(a.positions, a.pos_is_i64, t0) : 0.0f;
+  float pos_next = n > 0 ? load_position(a.positions, a.pos_is_i64, wu.at(0)) : 0.0f;
 
   int64_t j = 0;
   for (; j < n; ++j) {
     const float pos = pos_next;
-    if (j + 1 < n) pos_next = load_position(a.positions, a.pos_is_i64, t0 + j + 1);
+    if (j + 1 < n) pos_next = load_position(a.positions, a.pos_is_i64, wu.at(j + 1));
 
     // The token's (cos, sin) table, shared by every head.
     for (int i = lane; i < kHalf; i += kWarpSize) {
       const float angle = __fmul_rn(pos, inv_sm[i]);
-      cos_sm[i] = cosf(angle);
-      sin_sm[i] = sinf(angle);
+      sincosf(angle, &sin_sm[i], &cos_sm[i]);
     }
     __syncwarp();
     LaneTrig<E> trig;
@@ -216,7 +215,7 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
     const uint32_t parity = static_cast<uint32_t>((j / a.stages) & 1);
     if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[stage], parity))) break;
     const uint8_t* st = ring + static_cast<size_t>(stage) * a.stage_bytes;
-    const int64_t t = t0 + j;
+    const int64_t t = wu.at(j);
 
     for (int h0 = 0; h0 < total_heads; h0 += kHeadsPerPass) {
       const int h = h0 + lane / G;
@@ -245,7 +244,8 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
         } else {
           total = __fadd_rn(group_sum<G>(p_lo), group_sum<G>(p_hi));
         }
-        const float inv_rms = rsqrtf(__fadd_rn(__fdiv_rn(total, static_cast<float>(kDim)), a.eps));
+        // sum / head_dim: head_dim is a power of two here, so the multiply is exact
+        const float inv_rms = rsqrtf(__fadd_rn(__fmul_rn(total, 1.0f / kDim), a.eps));
         lo = normalize_vec<E>(lo, inv_rms, is_q ? qw_lo : kw_lo);
         hi = normalize_vec<E>(hi, inv_rms, is_q ? qw_hi : kw_hi);
       }
@@ -408,6 +408,7 @@ int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
   a.num_kv_heads = static_cast<int>(num_kv_heads);
   a.head_dim = static_cast<int>(head_dim);
   a.pos_is_i64 = pos_type == SVLLM_INDEX_I64;
+  a.interleave = interleave_units() ? 1 : 0;
   a.eps = eps;
   a.err = err;
   std::memcpy(a.inv_freq, inv_freq, sizeof(float) * (head_dim / 2));

@@ -11,6 +11,13 @@
 //     otherwise (gate and up as the two halves of one [rows, 2 * inter] tensor, say) chunks stay
 //     inside a row. Each warp owns a ring of stages; lane 0 keeps cp.async.bulk loads of the
 //     next chunks of gate and up in flight, and the warp writes 16-byte vectors of out.
+//   * Table path (bf16, large batches): a bf16 gate takes only 65536 values, so round(silu(g))
+//     is a function of the gate's 16 bits. Each CTA first evaluates that function for every
+//     bf16 pattern with the same expf / IEEE-division code into a 128 KB shared-memory table,
+//     then the stream needs one table load and one packed bf16 multiply per element instead of
+//     ~30 instructions of accurate math: identical results, a fraction of the issue slots. The
+//     table costs 65536 evaluations per CTA, so it is used only when every CTA has many times
+//     that many elements to process.
 //   * Plain path for unaligned or odd-sized rows: grid-stride element loop, still on the GPU.
 #include <cuda_runtime.h>
 
@@ -37,8 +44,13 @@ struct SiluArgs {
   int64_t chunk;         // elements per unit
   int stages;
   int stage_bytes;       // gate chunk, then up chunk
+  int table_offset;      // table path: byte offset of the 65536-entry table
+  int interleave;        // unit order (WarpUnits)
   int ring_offset;
 };
+
+constexpr int kTableEntries = 65536;  // one per bf16 bit pattern
+constexpr int kTableBytes = kTableEntries * 2;
 
 __device__ __forceinline__ float silu(float g) {
   return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
@@ -69,10 +81,25 @@ __device__ __forceinline__ uint4 silu_mul_vec<F32>(const uint4& g, const uint4& 
   return pack<F32>(f);
 }
 
-template <class E>
+// out = round(table[g] * u) for one 16-byte vector, table[g] = round(silu(g)) for bf16 g.
+__device__ __forceinline__ uint4 silu_mul_vec_table(const uint4& g, const uint4& u,
+                                                    const uint16_t* table) {
+  uint32_t y[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t w = word(g, i);
+    const uint32_t s = static_cast<uint32_t>(table[w & 0xffffu]) |
+                       (static_cast<uint32_t>(table[w >> 16]) << 16);
+    y[i] = bf16x2_mul(s, word(u, i));
+  }
+  return make_uint4(y[0], y[1], y[2], y[3]);
+}
+
+template <class E, bool kTable>
 __global__ void __launch_bounds__(512) silu_bulk_kernel(const SiluArgs a) {
   using S = typename E::Storage;
   constexpr int kVec = E::kPerVec;
+  static_assert(!kTable || sizeof(S) == 2, "the table path is for bf16");
   extern __shared__ __align__(128) uint8_t smem[];
 
   const int warps = blockDim.x / kWarpSize;
@@ -81,19 +108,30 @@ __global__ void __launch_bounds__(512) silu_bulk_kernel(const SiluArgs a) {
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * a.stages;
   uint8_t* ring = smem + a.ring_offset + static_cast<size_t>(warp) * a.stages * a.stage_bytes;
   const uint32_t half_stage = static_cast<uint32_t>(a.chunk * sizeof(S));
+  const uint16_t* table = reinterpret_cast<const uint16_t*>(smem + a.table_offset);
 
   if (lane == 0) {
     for (int s = 0; s < a.stages; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
   }
-  __syncwarp();
+  if constexpr (kTable) {
+    // round(silu(g)) for every bf16 pattern g, two per 32-bit word
+    uint32_t* table_words = reinterpret_cast<uint32_t*>(smem + a.table_offset);
+    for (int w = threadIdx.x; w < kTableEntries / 2; w += blockDim.x) {
+      const float g0 = __uint_as_float(static_cast<uint32_t>(2 * w) << 16);
+      const float g1 = __uint_as_float(static_cast<uint32_t>(2 * w + 1) << 16);
+      table_words[w] = pack_bf16x2(silu(g0), silu(g1));
+    }
+    __syncthreads();
+  } else {
+    __syncwarp();
+  }
 
   const int64_t chunks_per_row = (a.cols + a.chunk - 1) / a.chunk;
   const int64_t num_units = a.rows * chunks_per_row;
-  int64_t u0, u1;
-  partition(num_units, static_cast<int64_t>(gridDim.x) * warps,
-            static_cast<int64_t>(blockIdx.x) * warps + warp, u0, u1);
-  const int64_t n = u1 - u0;
+  const WarpUnits wu = warp_units(num_units, static_cast<int64_t>(gridDim.x) * warps,
+                                  static_cast<int64_t>(blockIdx.x) * warps + warp, a.interleave);
+  const int64_t n = wu.count;
 
   auto unit_of = [&](int64_t u, int64_t& row, int64_t& col, int& len) {
     row = u / chunks_per_row;
@@ -106,7 +144,7 @@ __global__ void __launch_bounds__(512) silu_bulk_kernel(const SiluArgs a) {
     uint8_t* st = ring + static_cast<size_t>(s) * a.stage_bytes;
     int64_t row, col;
     int len;
-    unit_of(u0 + j, row, col, len);
+    unit_of(wu.at(j), row, col, len);
     const uint32_t bytes = static_cast<uint32_t>(len) * sizeof(S);
     mbar_arrive_expect_tx(&bars[s], 2 * bytes);
     bulk_load(st, static_cast<const S*>(a.gate) + row * a.gate_stride + col, bytes, &bars[s]);
@@ -126,13 +164,18 @@ __global__ void __launch_bounds__(512) silu_bulk_kernel(const SiluArgs a) {
     const uint8_t* st = ring + static_cast<size_t>(s) * a.stage_bytes;
     int64_t row, col;
     int len;
-    unit_of(u0 + j, row, col, len);
+    unit_of(wu.at(j), row, col, len);
     S* out = static_cast<S*>(a.out) + row * a.out_stride + col;
     const int nv = len / kVec;
 #pragma unroll 2
     for (int v = lane; v < nv; v += kWarpSize) {
-      st_global_v4(out + v * kVec, silu_mul_vec<E>(ld_shared_v4(st + v * 16),
-                                                   ld_shared_v4(st + half_stage + v * 16)));
+      const uint4 g = ld_shared_v4(st + v * 16);
+      const uint4 u = ld_shared_v4(st + half_stage + v * 16);
+      if constexpr (kTable) {
+        st_global_v4(out + v * kVec, silu_mul_vec_table(g, u, table));
+      } else {
+        st_global_v4(out + v * kVec, silu_mul_vec<E>(g, u));
+      }
     }
     __syncwarp();
     if (lane == 0 && j + a.stages < n) {
@@ -190,6 +233,7 @@ int launch_silu(void* out, const void* gate, const void* up, int64_t num_rows, i
   a.gate = gate;
   a.up = up;
   a.err = err;
+  a.interleave = interleave_units() ? 1 : 0;
   const bool flat = out_stride == inter && gate_stride == inter && up_stride == inter;
   a.rows = flat ? 1 : num_rows;
   a.cols = flat ? num_rows * inter : inter;
@@ -207,20 +251,25 @@ int launch_silu(void* out, const void* gate, const void* up, int64_t num_rows, i
     chunk = std::min<int64_t>(chunk, round_up(a.cols, kVec));
     a.chunk = chunk;
     a.stage_bytes = static_cast<int>(round_up(2 * chunk * static_cast<int64_t>(sizeof(S)), 128));
+    // The table pays for itself once every CTA has many times 65536 elements to process.
+    const bool table = sizeof(S) == 2 &&
+                       a.rows * a.cols >= static_cast<int64_t>(sm_count(device)) * 4 * kTableEntries;
+    const int64_t table_bytes = table ? kTableBytes : 0;
     int warps = shape.warps;
     int stages = shape.stages;
     auto smem_for = [&](int w, int s) {
-      return round_up(static_cast<int64_t>(w) * s * 8, 128) +
+      return round_up(static_cast<int64_t>(w) * s * 8, 128) + table_bytes +
              static_cast<int64_t>(w) * s * a.stage_bytes;
     };
     while (smem_for(warps, stages) > static_cast<int64_t>(kMaxSmemPerCta) && stages > 2) --stages;
     while (smem_for(warps, stages) > static_cast<int64_t>(kMaxSmemPerCta) && warps > 1) --warps;
     if (smem_for(warps, stages) <= static_cast<int64_t>(kMaxSmemPerCta)) {
       a.stages = stages;
-      a.ring_offset = static_cast<int>(round_up(static_cast<int64_t>(warps) * stages * 8, 128));
+      a.table_offset = static_cast<int>(round_up(static_cast<int64_t>(warps) * stages * 8, 128));
+      a.ring_offset = a.table_offset + static_cast<int>(table_bytes);
       const size_t smem = static_cast<size_t>(smem_for(warps, stages));
       const int threads = warps * kWarpSize;
-      const auto kernel = silu_bulk_kernel<E>;
+      const auto kernel = table ? silu_bulk_kernel<E, sizeof(S) == 2> : silu_bulk_kernel<E, false>;
       const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(kernel), threads, smem, device);
       if (per_sm > 0) {
         const int64_t units = a.rows * ((a.cols + chunk - 1) / chunk);

@@ -327,3 +327,21 @@ def test_pipeline_shape_does_not_change_results(cuda, unit, stages, warps):
         for op in ("rms_norm", "silu_and_mul"):
             capi.set_pipeline(op, 8192, 4, 4)
     assert torch.equal(out, base) and torch.equal(sout, sbase)
+
+
+def test_silu_table_path_is_exhaustively_identical(cuda):
+    """Every one of the 65536 bf16 gate patterns (NaNs and infinities included) through the
+    table path (a batch large enough to take it) and through the direct path (one row, too small
+    for the table) gives the same bits, and the same bits as torch's silu * up on the GPU."""
+    patterns = torch.arange(-32768, 32768, dtype=torch.int32).to(torch.int16).view(torch.bfloat16)
+    reps = 640  # 640 * 65536 elements: above the table path's threshold on a B200
+    gate = patterns.to(cuda).repeat(reps).view(reps, 65536)
+    up = random_t(reps, 65536, device=cuda, seed=30)
+    out = torch.empty_like(gate)
+    capi.silu_and_mul(out, gate, up)
+    small = torch.empty(1, 65536, dtype=torch.bfloat16, device=cuda)
+    capi.silu_and_mul(small, gate[:1], up[:1])
+    expect = F.silu(gate) * up
+    bits = lambda t: t.view(torch.int16)  # noqa: E731  (NaN == NaN as bit patterns)
+    assert torch.equal(bits(out[:1]), bits(small)), "table path != direct path"
+    assert torch.equal(bits(out), bits(expect)), "table path != torch silu * up"
