@@ -72,6 +72,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-validate", action="store_true")
     p.add_argument("--cpu-sample-tokens", type=int, default=32768)
+    p.add_argument("--graph", action="store_true",
+                   help="capture the chain in a CUDA graph and time replays (small-T regime)")
     return p.parse_args()
 
 
@@ -378,6 +380,20 @@ def main() -> int:
     assert svllm_ops.read_device_error(local, True) == 0
 
     ev = {op: [] for op in OPS}
+    graph = None
+    if args.graph:
+        # one graph holds the whole chain: the launch latency of four kernels becomes one replay
+        graph = torch.cuda.CUDAGraph()
+        capture = torch.cuda.Stream()
+        capture.wait_stream(stream)
+        with torch.cuda.stream(capture):
+            with torch.cuda.graph(graph, stream=capture):
+                for op in OPS:
+                    chain.run_op(op)
+        stream.wait_stream(capture)
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
     sampler = ClockSampler(list(range(world)) if world > 1 else [local], enabled=rank == 0)
     barrier()
     torch.cuda.synchronize()
@@ -386,6 +402,9 @@ def main() -> int:
         stop = torch.cuda.Event(enable_timing=True)
         start.record(stream)
         for _ in range(args.steps):
+            if graph is not None:
+                graph.replay()
+                continue
             for op in OPS:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
@@ -397,6 +416,18 @@ def main() -> int:
         torch.cuda.synchronize()
     barrier()
     elapsed_ms = start.elapsed_time(stop)
+    if graph is not None:
+        # per-op times come from an eager pass of the same ops (a replay has no per-op events)
+        for _ in range(args.steps):
+            for op in OPS:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                chain.run_op(op)
+                e1.record(stream)
+                ev[op].append((e0, e1))
+        torch.cuda.synchronize()
+        del graph
     op_ms = {op: sum(a.elapsed_time(b) for a, b in ev[op]) / args.steps for op in OPS}
 
     t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
@@ -448,6 +479,7 @@ def main() -> int:
                          if not peaks.get("fallback") else "fallback 6650 GB/s"},
             "clocks": clocks,
             "gpu_launches": len(OPS) * args.steps,
+            "cuda_graph": bool(args.graph),
             "e2e": e2e,
             "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
             if cpu else None,

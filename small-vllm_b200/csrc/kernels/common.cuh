@@ -240,14 +240,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// One bounded try: the thread may sleep (without issuing) until the phase completes or the
+// suspend-time hint (ns) passes, so a warp waiting on HBM costs almost no issue slots.
+constexpr uint32_t kTryWaitSuspendNs = 1000000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "n"(kTryWaitSuspendNs)
       : "memory");
   return done != 0;
 }
@@ -326,7 +330,9 @@ __device__ __forceinline__ float group_sum(float v) {
 
 // The units a warp processes: a contiguous, balanced share of n units (interleave = false), or
 // every warps_total-th unit starting at the warp's index (interleave = true), so that at any
-// moment the grid streams through neighbouring units of memory together.
+// moment the grid streams through neighbouring units of memory together. On a B200 at 1M tokens
+// the interleaved order measured 1-4% faster for the norm, rotary and SiLU kernels; the gather
+// keeps contiguous shares so that a warp's ids arrive in coalesced batches.
 struct WarpUnits {
   int64_t first;
   int64_t step;

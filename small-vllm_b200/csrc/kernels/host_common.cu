@@ -2,7 +2,6 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
-#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -28,12 +27,12 @@ std::atomic<int*> g_error_word[kMaxDevices];
 // needs at ~1 us of memory latency; the compute-heavier ops (SiLU, q/k norm + RoPE) also want
 // many resident warps to hide their latency chains.
 PipelineShape g_shapes[static_cast<int>(OpId::kCount)] = {
-    {8192, 2, 12},  // rms_norm
-    {8192, 3, 8},   // add_rms_norm
+    {8192, 2, 8},   // rms_norm
+    {4096, 4, 8},   // add_rms_norm
     {4096, 2, 16},  // qk_norm_rope (a unit is one token; unit_bytes is unused)
     {4096, 2, 16},  // rope
-    {4096, 2, 12},  // silu_and_mul
-    {4096, 2, 16},  // embedding (a unit is one row; unit_bytes is unused)
+    {8192, 2, 6},   // silu_and_mul (the table path leaves ~99 KB of shared memory for stages)
+    {4096, 3, 4},   // embedding (a unit is one row; unit_bytes is unused)
 };
 
 const char* const kOpNames[] = {"rms_norm", "add_rms_norm", "qk_norm_rope",
@@ -128,14 +127,6 @@ int blocks_per_sm(const void* func, int threads, size_t smem_bytes, int device) 
   }
   if (g_occ_used < kOccCacheSize) g_occ[g_occ_used++] = {func, threads, smem_bytes, device, blocks};
   return blocks;
-}
-
-bool interleave_units() {
-  static const bool on = [] {
-    const char* v = std::getenv("SVLLM_INTERLEAVE");
-    return v != nullptr && v[0] == '1';
-  }();
-  return on;
 }
 
 int* library_error_word(int device) {

@@ -34,10 +34,6 @@ int blocks_per_sm(const void* func, int threads, size_t smem_bytes, int device);
 // Largest dynamic shared memory a CTA may use on this architecture.
 constexpr size_t kMaxSmemPerCta = 227 * 1024;
 
-// Work assignment of the streaming kernels (see WarpUnits): SVLLM_INTERLEAVE=1 selects the
-// interleaved order. Read once.
-bool interleave_units();
-
 // The library's own error word on `device` (a __device__ int, address cached per device).
 int* library_error_word(int device);
 

@@ -408,7 +408,7 @@ int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
   a.num_kv_heads = static_cast<int>(num_kv_heads);
   a.head_dim = static_cast<int>(head_dim);
   a.pos_is_i64 = pos_type == SVLLM_INDEX_I64;
-  a.interleave = interleave_units() ? 1 : 0;
+  a.interleave = 1;  // measured faster than contiguous shares on B200
   a.eps = eps;
   a.err = err;
   std::memcpy(a.inv_freq, inv_freq, sizeof(float) * (head_dim / 2));

@@ -233,7 +233,7 @@ int launch_silu(void* out, const void* gate, const void* up, int64_t num_rows, i
   a.gate = gate;
   a.up = up;
   a.err = err;
-  a.interleave = interleave_units() ? 1 : 0;
+  a.interleave = 1;  // measured faster than contiguous shares on B200
   const bool flat = out_stride == inter && gate_stride == inter && up_stride == inter;
   a.rows = flat ? 1 : num_rows;
   a.cols = flat ? num_rows * inter : inter;
