@@ -32,8 +32,12 @@ sys.path[:0] = [str(ROOT / "small-vllm_b200" / "python"), str(ROOT / "oracle")]
 METRIC = "fused layer-op achieved HBM GB/s (% of B200 peak) and tokens/s at 1/2/4/8 GPUs"
 UNIT = "GB/s"
 
-QWEN3 = dict(hidden=1024, heads=16, kv_heads=8, head_dim=128, inter=3072, vocab=151936,
-             eps=1e-6, theta=1e6)
+QWEN3 = dict(name="qwen3-0.6b", hidden=1024, heads=16, kv_heads=8, head_dim=128, inter=3072,
+             vocab=151936, eps=1e-6, theta=1e6, qk_norm=True, scaling=None)
+# Llama-3.2-1B; the benchmark definition states llama3 scaling factor 32 (the model's config.json
+# has 8.0; the formula is the same and both are tested)
+LLAMA = dict(name="llama-3.2-1b", hidden=2048, heads=32, kv_heads=8, head_dim=64, inter=8192,
+             vocab=128256, eps=1e-5, theta=5e5, qk_norm=False, scaling=(32.0, 1.0, 4.0, 8192))
 
 # Algorithmic bytes per token of each op (bf16 activations; int32 ids; int64 positions):
 #   embedding     read the table row and write the output row, plus the id
@@ -46,18 +50,24 @@ def op_bytes(cfg: dict) -> dict[str, int]:
     return {
         "embedding": 2 * h * 2 + 4,
         "add_rms_norm": 4 * h * 2,
-        "qk_norm_rope": 2 * heads * hd * 2 + 8,
+        "qk_norm_rope" if cfg["qk_norm"] else "rope": 2 * heads * hd * 2 + 8,
         "silu_and_mul": 3 * inter * 2,
     }
 
 
 OPS = ["embedding", "add_rms_norm", "qk_norm_rope", "silu_and_mul"]
 WORKLOADS = {
-    # name: (total tokens, position range)
-    "sweep": (1_048_576, 32768),
-    "prefill": (70_000, 2048),
-    "decode": (256, 4096),
+    # name: (model, total tokens, positions: ("uniform", hi) or ("packed", sequence length))
+    "sweep": (QWEN3, 1_048_576, ("uniform", 32768)),
+    "prefill": (QWEN3, 70_000, ("uniform", 2048)),
+    "decode": (QWEN3, 256, ("uniform", 4096)),
+    "llama": (LLAMA, 16_384, ("packed", 2048)),
 }
+
+
+def op_names(cfg: dict) -> list[str]:
+    """The chain's ops; Llama has no q/k norm, so its rotary step is rope alone."""
+    return [op if op != "qk_norm_rope" or cfg["qk_norm"] else "rope" for op in OPS]
 
 
 def parse_args():
@@ -94,7 +104,7 @@ def split_rows(total: int, world: int, rank: int) -> tuple[int, int]:
 # ---------------------------------------------------------------------------------------------
 # Synthetic inputs (seeded, per rank)
 
-def make_inputs(T: int, pos_hi: int, cfg: dict, device, seed: int):
+def make_inputs(T: int, pos_spec: tuple, cfg: dict, device, seed: int, first_row: int = 0):
     import torch
 
     g = torch.Generator(device=device).manual_seed(seed)
@@ -114,7 +124,9 @@ def make_inputs(T: int, pos_hi: int, cfg: dict, device, seed: int):
         "k": randn(T, cfg["kv_heads"], hd),
         "qw": randn(hd, scale=0.1, shift=1.0),
         "kw": randn(hd, scale=0.1, shift=1.0),
-        "pos": torch.randint(0, pos_hi, (T,), device=device, dtype=torch.int64, generator=g),
+        "pos": (torch.randint(0, pos_spec[1], (T,), device=device, dtype=torch.int64, generator=g)
+                if pos_spec[0] == "uniform" else
+                (torch.arange(first_row, first_row + T, device=device) % pos_spec[1])),
         "gate": randn(T, cfg["inter"]),
         "up": randn(T, cfg["inter"]),
     }
@@ -141,9 +153,18 @@ class Chain:
         elif name == "add_rms_norm":
             o.add_rms_norm(i["x"], i["residual"], i["w"], c["eps"])
         elif name == "qk_norm_rope":
-            o.qk_norm_rope(i["q"], i["k"], i["qw"], i["kw"], i["pos"], c["eps"], c["theta"])
+            o.qk_norm_rope(i["q"], i["k"], i["qw"], i["kw"], i["pos"], c["eps"], c["theta"],
+                           scaling_of(c))
+        elif name == "rope":
+            o.rope(i["q"], i["k"], i["pos"], c["theta"], scaling_of(c))
         else:
             self.silu_out = o.silu_and_mul(i["gate"], i["up"])
+
+
+def scaling_of(cfg: dict):
+    import svllm_ops
+
+    return svllm_ops.Llama3RopeScaling(*cfg["scaling"]) if cfg["scaling"] else None
 
 
 # ---------------------------------------------------------------------------------------------
@@ -221,7 +242,8 @@ class ClockSampler:
 # (built from its sources into oracle/_ref) where the reference has the op, and the C/OpenMP
 # restatement (oracle/) for the rest. Host-resident, all host threads.
 
-def cpu_chain_sample(tokens: int, cfg: dict, pos_hi: int, steps: int, min_seconds: float = 0.0):
+def cpu_chain_sample(tokens: int, cfg: dict, pos_spec: tuple, steps: int,
+                     min_seconds: float = 0.0):
     import numpy as np
     import torch
 
@@ -241,16 +263,18 @@ def cpu_chain_sample(tokens: int, cfg: dict, pos_hi: int, steps: int, min_second
     x, r, w = bf16(tokens, h), bf16(tokens, h), bf16(h, scale=0.1, shift=1.0)
     q, k = bf16(tokens, cfg["heads"], hd), bf16(tokens, cfg["kv_heads"], hd)
     qw, kw = bf16(hd, scale=0.1, shift=1.0), bf16(hd, scale=0.1, shift=1.0)
-    pos = rng.integers(0, pos_hi, tokens, dtype=np.int64)
+    pos = (rng.integers(0, pos_spec[1], tokens, dtype=np.int64) if pos_spec[0] == "uniform"
+           else np.arange(tokens, dtype=np.int64) % pos_spec[1])
     gate, up = bf16(tokens, inter), bf16(tokens, inter)
-    inv = oracle.inv_freq(cfg["theta"], hd)
+    inv = oracle.inv_freq(cfg["theta"], hd, cfg["scaling"])
+    names = op_names(cfg)
 
     def as_t(a):
         return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16)
 
     tx, tr, tw, tq, tk = as_t(x), as_t(r), as_t(w), as_t(q), as_t(k)
     tqw, tkw = as_t(qw), as_t(kw)
-    per_op = {op: 0.0 for op in OPS}
+    per_op = {op: 0.0 for op in names}
     done = 0
     t_start = time.perf_counter()
     while done < steps or time.perf_counter() - t_start < min_seconds:
@@ -263,7 +287,9 @@ def cpu_chain_sample(tokens: int, cfg: dict, pos_hi: int, steps: int, min_second
         else:
             oracle.add_rms_norm(x, r, w, cfg["eps"], inplace=True)
         t2 = time.perf_counter()
-        if ref is not None:
+        if not cfg["qk_norm"]:
+            oracle.rope(q, k, pos, inv, inplace=True)
+        elif ref is not None:
             qn = ref.rms_norm(tq.view(-1, hd), tqw, cfg["eps"])
             kn = ref.rms_norm(tk.view(-1, hd), tkw, cfg["eps"])
             oracle.rope(qn.view(torch.int16).numpy().view(np.uint16).reshape(q.shape),
@@ -274,7 +300,7 @@ def cpu_chain_sample(tokens: int, cfg: dict, pos_hi: int, steps: int, min_second
         t3 = time.perf_counter()
         oracle.silu_and_mul(gate, up)
         t4 = time.perf_counter()
-        for op, dt in zip(OPS, (t1 - t0, t2 - t1, t3 - t2, t4 - t3)):
+        for op, dt in zip(names, (t1 - t0, t2 - t1, t3 - t2, t4 - t3)):
             per_op[op] += dt
         done += 1
     nbytes = op_bytes(cfg)
@@ -285,7 +311,7 @@ def cpu_chain_sample(tokens: int, cfg: dict, pos_hi: int, steps: int, min_second
               + ("reference's own OpenMP rms_norm (oracle/_ref, built from its sources) for the "
                  "norms, after a LibTorch add; C/OpenMP restatement (oracle/) for embedding, "
                  "rope, silu_and_mul" if ref is not None else "C/OpenMP restatement (oracle/)"))
-    ops = {op: round(nbytes[op] * tokens * done / per_op[op] / 1e9, 2) for op in OPS}
+    ops = {op: round(nbytes[op] * tokens * done / per_op[op] / 1e9, 2) for op in names}
     return {"value": round(gbs, 2), "unit": UNIT, "cores": cores, "kind": kind, "sample": sample,
             "ops_gbs": ops, "tokens_per_s": round(tokens * done / total_s, 1),
             "ms_per_step": round(1e3 * total_s / done, 3)}
@@ -313,22 +339,21 @@ def dist_setup(args):
 
 
 def run_reference(args, world, rank) -> int:
-    cfg = QWEN3
-    total, pos_hi = WORKLOADS[args.workload]
+    cfg, total, pos_spec = WORKLOADS[args.workload]
     total = args.tokens or total
     if rank != 0:
         return 0
     tokens = min(args.cpu_sample_tokens, total)
     # untimed warm-up passes, then exactly `steps` timed passes
-    cpu_chain_sample(min(tokens, 4096), cfg, pos_hi, max(1, args.warmup))
-    base = cpu_chain_sample(tokens, cfg, pos_hi, args.steps)
+    cpu_chain_sample(min(tokens, 4096), cfg, pos_spec, max(1, args.warmup))
+    base = cpu_chain_sample(tokens, cfg, pos_spec, args.steps)
     line = {
         "metric": METRIC, "value": base["value"], "unit": UNIT, "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": base["ms_per_step"], "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"qwen3-0.6b layer-op chain, {args.workload}", "tokens": total,
-                   "sample_tokens": tokens, "ops": OPS},
+        "config": {"workload": f"{cfg['name']} layer-op chain, {args.workload}", "tokens": total,
+                   "sample_tokens": tokens, "ops": op_names(cfg)},
         "tokens_per_s": base["tokens_per_s"], "ops_gbs": base["ops_gbs"],
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -352,15 +377,15 @@ def main() -> int:
     assert torch.cuda.is_available(), "bench.py (impl ours) needs a GPU"
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    cfg = QWEN3
-    total, pos_hi = WORKLOADS[args.workload]
+    cfg, total, pos_spec = WORKLOADS[args.workload]
     total = args.tokens or total
+    names = op_names(cfg)
     begin, end = split_rows(total, world, rank)
     T = end - begin
     nbytes = op_bytes(cfg)
     chain_bytes_per_token = sum(nbytes.values())
 
-    inp = make_inputs(T, pos_hi, cfg, dev, seed=1000 + rank)
+    inp = make_inputs(T, pos_spec, cfg, dev, seed=1000 + rank, first_row=begin)
     chain = Chain(inp, cfg)
     torch.cuda.synchronize()
 
@@ -374,12 +399,12 @@ def main() -> int:
 
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
-        for op in OPS:
+        for op in names:
             chain.run_op(op)
     torch.cuda.synchronize()
     assert svllm_ops.read_device_error(local, True) == 0
 
-    ev = {op: [] for op in OPS}
+    ev = {op: [] for op in names}
     graph = None
     if args.graph:
         # one graph holds the whole chain: the launch latency of four kernels becomes one replay
@@ -388,7 +413,7 @@ def main() -> int:
         capture.wait_stream(stream)
         with torch.cuda.stream(capture):
             with torch.cuda.graph(graph, stream=capture):
-                for op in OPS:
+                for op in names:
                     chain.run_op(op)
         stream.wait_stream(capture)
         for _ in range(args.warmup):
@@ -405,7 +430,7 @@ def main() -> int:
             if graph is not None:
                 graph.replay()
                 continue
-            for op in OPS:
+            for op in names:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
@@ -419,7 +444,7 @@ def main() -> int:
     if graph is not None:
         # per-op times come from an eager pass of the same ops (a replay has no per-op events)
         for _ in range(args.steps):
-            for op in OPS:
+            for op in names:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e1 = torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
@@ -428,7 +453,7 @@ def main() -> int:
                 ev[op].append((e0, e1))
         torch.cuda.synchronize()
         del graph
-    op_ms = {op: sum(a.elapsed_time(b) for a, b in ev[op]) / args.steps for op in OPS}
+    op_ms = {op: sum(a.elapsed_time(b) for a, b in ev[op]) / args.steps for op in names}
 
     t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
     if world > 1:
@@ -442,15 +467,15 @@ def main() -> int:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_chain_sample(min(args.cpu_sample_tokens, total), cfg, pos_hi, 2,
+        cpu = cpu_chain_sample(min(args.cpu_sample_tokens, total), cfg, pos_spec, 2,
                                min_seconds=5.0)
 
     if rank == 0:
         peaks = measured_peaks()
         peak = float(peaks["hbm_gbs"])
         value = chain_bytes_per_token * total / (max_ms * 1e-3) / 1e9
-        ops_gbs = {op: round(nbytes[op] * T / (op_ms[op] * 1e-3) / 1e9, 1) for op in OPS}
-        dominant = max(OPS, key=lambda op: op_ms[op])
+        ops_gbs = {op: round(nbytes[op] * T / (op_ms[op] * 1e-3) / 1e9, 1) for op in names}
+        dominant = max(names, key=lambda op: op_ms[op])
         traffic = load_traffic(dominant, T)
         achieved = nbytes[dominant] * T / (op_ms[dominant] * 1e-3) / 1e9
         clocks = sampler.summary()
@@ -459,18 +484,20 @@ def main() -> int:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(max_ms, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"qwen3-0.6b layer-op chain, {args.workload}",
+            "config": {"workload": f"{cfg['name']} layer-op chain, {args.workload}",
                        "tokens": total, "tokens_per_gpu": T, "hidden": cfg["hidden"],
                        "heads": [cfg["heads"], cfg["kv_heads"]], "head_dim": cfg["head_dim"],
                        "intermediate": cfg["inter"], "vocab": cfg["vocab"],
-                       "positions": f"uniform [0, {pos_hi})", "ops": OPS,
+                       "positions": (f"uniform [0, {pos_spec[1]})" if pos_spec[0] == "uniform"
+                                     else f"sequences of {pos_spec[1]}, positions 0..{pos_spec[1] - 1}"),
+                       "rope_scaling": cfg["scaling"], "ops": names,
                        "l2": "no flush: every op's inputs exceed the 126 MB L2"
                        if T * 2 * cfg["hidden"] > 126e6 else "inputs L2-resident (small T)",
                        "parallelism": f"rows sharded over {world} GPU(s), no collective"},
             "tokens_per_s": round(total / (max_ms * 1e-3), 1),
             "frac_of_peak": round(value / (peak * world), 4),
             "ops_gbs_per_gpu": ops_gbs,
-            "ops_ms_per_gpu": {op: round(op_ms[op], 4) for op in OPS},
+            "ops_ms_per_gpu": {op: round(op_ms[op], 4) for op in names},
             "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic,
@@ -478,7 +505,7 @@ def main() -> int:
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"
                          if not peaks.get("fallback") else "fallback 6650 GB/s"},
             "clocks": clocks,
-            "gpu_launches": len(OPS) * args.steps,
+            "gpu_launches": len(names) * args.steps,
             "cuda_graph": bool(args.graph),
             "e2e": e2e,
             "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
@@ -527,7 +554,7 @@ def validate(chain, inp, cfg, world, rank, dev, rows: int = 256):
         n = int(t.item())
     saved = {k: inp[k][:n].clone() for k in ("ids", "x", "residual", "q", "k", "pos", "gate",
                                             "up")}
-    for op in OPS:
+    for op in op_names(cfg):
         chain.run_op(op)
     torch.cuda.synchronize()
     got = {"embedding": chain.emb_out[:n], "x": inp["x"][:n], "residual": inp["residual"][:n],
@@ -546,7 +573,11 @@ def validate(chain, inp, cfg, world, rank, dev, rows: int = 256):
     x, r = ins["x"].clone(), ins["residual"].clone()
     ops.add_rms_norm(x, r, inp["w"].cpu(), cfg["eps"])
     q, k = ins["q"].clone(), ins["k"].clone()
-    ops.qk_norm_rope(q, k, inp["qw"].cpu(), inp["kw"].cpu(), ins["pos"], cfg["eps"], cfg["theta"])
+    if cfg["qk_norm"]:
+        ops.qk_norm_rope(q, k, inp["qw"].cpu(), inp["kw"].cpu(), ins["pos"], cfg["eps"],
+                         cfg["theta"], scaling_of(cfg))
+    else:
+        ops.rope(q, k, ins["pos"], cfg["theta"], scaling_of(cfg))
     y = ops.silu_and_mul(ins["gate"], ins["up"])
     want = {"embedding": emb, "x": x, "residual": r, "q": q, "k": k, "silu": y}
 
@@ -622,8 +653,12 @@ def measure_e2e(chain, inp, cfg, args, world, dev):
             emb = svllm_ops.embedding(inp["ids"][a:b], inp["table"])
             emb_dev[a:b].copy_(emb, non_blocking=True)
             svllm_ops.add_rms_norm(inp["x"][a:b], inp["residual"][a:b], inp["w"], cfg["eps"])
-            svllm_ops.qk_norm_rope(inp["q"][a:b], inp["k"][a:b], inp["qw"], inp["kw"],
-                                   inp["pos"][a:b], cfg["eps"], cfg["theta"])
+            if cfg["qk_norm"]:
+                svllm_ops.qk_norm_rope(inp["q"][a:b], inp["k"][a:b], inp["qw"], inp["kw"],
+                                       inp["pos"][a:b], cfg["eps"], cfg["theta"], scaling_of(cfg))
+            else:
+                svllm_ops.rope(inp["q"][a:b], inp["k"][a:b], inp["pos"][a:b], cfg["theta"],
+                               scaling_of(cfg))
             silu_dev[a:b].copy_(svllm_ops.silu_and_mul(inp["gate"][a:b], inp["up"][a:b]),
                                 non_blocking=True)
             e = torch.cuda.Event()
