@@ -105,25 +105,28 @@ def split_rows(total: int, world: int, rank: int) -> tuple[int, int]:
 # Synthetic inputs (seeded, per rank)
 
 def make_inputs(T: int, pos_spec: tuple, cfg: dict, device, seed: int, first_row: int = 0):
+    """Per-rank activations from `seed`; the weights (embedding table, norm weights) from one
+    fixed seed, so every rank holds the same replicated model weights."""
     import torch
 
     g = torch.Generator(device=device).manual_seed(seed)
+    gw = torch.Generator(device=device).manual_seed(1234)
 
-    def randn(*shape, scale=1.0, shift=0.0):
+    def randn(*shape, scale=1.0, shift=0.0, gen=g):
         t = torch.empty(shape, device=device, dtype=torch.bfloat16)
-        return t.normal_(shift, scale, generator=g) if shape[0] else t
+        return t.normal_(shift, scale, generator=gen) if shape[0] else t
 
     h, hd = cfg["hidden"], cfg["head_dim"]
     return {
-        "table": randn(cfg["vocab"], h, scale=0.02),
+        "table": randn(cfg["vocab"], h, scale=0.02, gen=gw),
+        "w": randn(h, scale=0.1, shift=1.0, gen=gw),
+        "qw": randn(hd, scale=0.1, shift=1.0, gen=gw),
+        "kw": randn(hd, scale=0.1, shift=1.0, gen=gw),
         "ids": torch.randint(0, cfg["vocab"], (T,), device=device, dtype=torch.int32, generator=g),
         "x": randn(T, h),
         "residual": randn(T, h),
-        "w": randn(h, scale=0.1, shift=1.0),
         "q": randn(T, cfg["heads"], hd),
         "k": randn(T, cfg["kv_heads"], hd),
-        "qw": randn(hd, scale=0.1, shift=1.0),
-        "kw": randn(hd, scale=0.1, shift=1.0),
         "pos": (torch.randint(0, pos_spec[1], (T,), device=device, dtype=torch.int64, generator=g)
                 if pos_spec[0] == "uniform" else
                 (torch.arange(first_row, first_row + T, device=device) % pos_spec[1])),

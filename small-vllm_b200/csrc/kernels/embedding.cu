@@ -193,7 +193,7 @@ int launch_embedding(void* out, const void* ids, int id_type, const void* table,
   if (bulk_ok) {
     const PipelineShape shape = pipeline_shape(OpId::kEmbedding);
     a.stage_bytes = static_cast<int>(round_up(a.row_bytes, 128));
-    int warps = shape.warps;
+    int warps = warps_for(num_tokens, shape.warps, device);
     int stages = shape.stages;
     auto smem_for = [&](int w, int s) {
       return round_up(static_cast<int64_t>(w) * s * 8, 128) +

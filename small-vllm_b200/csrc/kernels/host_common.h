@@ -47,6 +47,14 @@ inline int launch_status() {
   return e == cudaSuccess ? SVLLM_OK : SVLLM_ERR_LAUNCH;
 }
 
+// Warps per CTA for a batch of `units` work units: the tuned count, or fewer when the batch is
+// too small to give every SM a full CTA (decode-sized batches), so that the grid still spans
+// all SMs and each warp's latency chain starts at once.
+inline int warps_for(int64_t units, int tuned, int device) {
+  const int64_t per_sm = (units + sm_count(device) - 1) / sm_count(device);
+  return static_cast<int>(per_sm < tuned ? (per_sm > 0 ? per_sm : 1) : tuned);
+}
+
 // Grid size for a persistent kernel: enough CTAs to fill every SM at the given occupancy, but
 // no more CTAs than there is work for.
 inline int64_t persistent_grid(int64_t work_ctas, int device, int per_sm) {

@@ -355,7 +355,7 @@ int launch_norm(void* out, const void* x, void* residual, const void* weight, in
       rows = std::min<int64_t>(rows, round_up(num_rows, rows_per_pass));
       a.rows_per_unit = static_cast<int>(rows);
       a.stage_bytes = static_cast<int>(round_up(rows * unit_row_bytes, 128));
-      int warps = shape.warps;
+      int warps = warps_for((num_rows + rows - 1) / rows, shape.warps, device);
       int stages = shape.stages;
       auto smem_for = [&](int w, int s) {
         return round_up(static_cast<int64_t>(w) * s * 8, 128) + round_up(row_bytes, 128) +

@@ -427,7 +427,7 @@ int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
   if (kernel != nullptr) {
     const PipelineShape shape = pipeline_shape(kNorm ? OpId::kQkNormRope : OpId::kRope);
     a.stage_bytes = static_cast<int>(round_up(q_bytes + k_bytes, 128));
-    int warps = shape.warps;
+    int warps = warps_for(num_tokens, shape.warps, device);
     int stages = shape.stages;
     const int64_t half = head_dim / 2;
     auto smem_for = [&](int w, int s) {

@@ -255,7 +255,7 @@ int launch_silu(void* out, const void* gate, const void* up, int64_t num_rows, i
     const bool table = sizeof(S) == 2 &&
                        a.rows * a.cols >= static_cast<int64_t>(sm_count(device)) * 4 * kTableEntries;
     const int64_t table_bytes = table ? kTableBytes : 0;
-    int warps = shape.warps;
+    int warps = warps_for(a.rows * ((a.cols + chunk - 1) / chunk), shape.warps, device);
     int stages = shape.stages;
     auto smem_for = [&](int w, int s) {
       return round_up(static_cast<int64_t>(w) * s * 8, 128) + table_bytes +
