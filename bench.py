@@ -47,10 +47,14 @@ LLAMA = dict(name="llama-3.2-1b", hidden=2048, heads=32, kv_heads=8, head_dim=64
 def op_bytes(cfg: dict) -> dict[str, int]:
     h, hd, inter = cfg["hidden"], cfg["head_dim"], cfg["inter"]
     heads = cfg["heads"] + cfg["kv_heads"]
+    kv_row = cfg["kv_heads"] * hd * 2
+    rotary = 2 * heads * hd * 2 + 8
+    if cfg.get("kv_cache"):
+        rotary += kv_row + 2 * kv_row + 8  # k into the cache; v read and written; the slot
     return {
         "embedding": 2 * h * 2 + 4,
         "add_rms_norm": 4 * h * 2,
-        "qk_norm_rope" if cfg["qk_norm"] else "rope": 2 * heads * hd * 2 + 8,
+        rotary_op(cfg): rotary,
         "silu_and_mul": 3 * inter * 2,
     }
 
@@ -65,9 +69,15 @@ WORKLOADS = {
 }
 
 
+def rotary_op(cfg: dict) -> str:
+    """Llama has no q/k norm, so its rotary step is rope alone; with a KV cache the step also
+    writes the cache."""
+    name = "qk_norm_rope" if cfg["qk_norm"] else "rope"
+    return name + "_cache" if cfg.get("kv_cache") else name
+
+
 def op_names(cfg: dict) -> list[str]:
-    """The chain's ops; Llama has no q/k norm, so its rotary step is rope alone."""
-    return [op if op != "qk_norm_rope" or cfg["qk_norm"] else "rope" for op in OPS]
+    return [rotary_op(cfg) if op == "qk_norm_rope" else op for op in OPS]
 
 
 def parse_args():
@@ -82,6 +92,9 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-validate", action="store_true")
     p.add_argument("--cpu-sample-tokens", type=int, default=32768)
+    p.add_argument("--kv-cache", action="store_true",
+                   help="the rotary step also writes k and v into a paged KV cache "
+                        "(qk_norm_rope_cache / rope_cache)")
     p.add_argument("--graph", action="store_true",
                    help="capture the chain in a CUDA graph and time replays (small-T regime)")
     return p.parse_args()
@@ -132,6 +145,26 @@ def make_inputs(T: int, pos_spec: tuple, cfg: dict, device, seed: int, first_row
                 (torch.arange(first_row, first_row + T, device=device) % pos_spec[1])),
         "gate": randn(T, cfg["inter"]),
         "up": randn(T, cfg["inter"]),
+        **(kv_inputs(T, cfg, device, g) if cfg.get("kv_cache") else {}),
+    }
+
+
+def kv_inputs(T: int, cfg: dict, device, g):
+    """v rows and a paged KV cache of 16-token blocks handed out in a random order, as an
+    allocator would after some churn; slot_mapping follows the blocks."""
+    import torch
+
+    block = 16
+    num_blocks = (T + block - 1) // block
+    perm = torch.randperm(num_blocks, device=device, generator=g)
+    t = torch.arange(T, device=device)
+    shape = (num_blocks * block, cfg["kv_heads"], cfg["head_dim"])
+    return {
+        "v": torch.empty(T, cfg["kv_heads"], cfg["head_dim"], device=device,
+                         dtype=torch.bfloat16).normal_(generator=g),
+        "slots": perm[t // block] * block + t % block,
+        "k_cache": torch.zeros(shape, device=device, dtype=torch.bfloat16),
+        "v_cache": torch.zeros(shape, device=device, dtype=torch.bfloat16),
     }
 
 
@@ -160,6 +193,12 @@ class Chain:
                            scaling_of(c))
         elif name == "rope":
             o.rope(i["q"], i["k"], i["pos"], c["theta"], scaling_of(c))
+        elif name == "qk_norm_rope_cache":
+            o.qk_norm_rope_cache(i["q"], i["k"], i["v"], i["qw"], i["kw"], i["pos"], i["slots"],
+                                 i["k_cache"], i["v_cache"], c["eps"], c["theta"], scaling_of(c))
+        elif name == "rope_cache":
+            o.rope_cache(i["q"], i["k"], i["v"], i["pos"], i["slots"], i["k_cache"],
+                         i["v_cache"], c["theta"], scaling_of(c))
         else:
             self.silu_out = o.silu_and_mul(i["gate"], i["up"])
 
@@ -382,6 +421,11 @@ def main() -> int:
     torch.cuda.set_device(dev)
     cfg, total, pos_spec = WORKLOADS[args.workload]
     total = args.tokens or total
+    if args.kv_cache:
+        # the cache variant is measured on the device; e2e, the CPU leg and validation cover the
+        # headline chain
+        cfg = dict(cfg, kv_cache=True)
+        args.no_e2e = args.no_cpu_baseline = args.no_validate = True
     names = op_names(cfg)
     begin, end = split_rows(total, world, rank)
     T = end - begin

@@ -55,7 +55,8 @@ typedef enum svllm_status {
 } svllm_status;
 
 /* Bits of the device error word. */
-#define SVLLM_DEVERR_BAD_INDEX 1    /* an embedding id outside [0, vocab): its row is zeroed */
+#define SVLLM_DEVERR_BAD_INDEX 1    /* an embedding id outside [0, vocab) (its row is zeroed) or a
+                                       KV slot past the cache (nothing written) */
 #define SVLLM_DEVERR_WAIT_TIMEOUT 2 /* a bulk copy did not land in time: the kernel stopped */
 
 /* Index dtype of positions / token ids. */
@@ -140,6 +141,47 @@ int svllm_rope_f32(float* q, float* k, const void* positions, int pos_type, int6
                    int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
                    int64_t q_row_stride, int64_t k_row_stride, const float* inv_freq,
                    svllm_stream stream);
+
+/*
+ * The two rotary ops fused with the paged-KV cache write that follows them in a decoder layer
+ * (the reference's AGENTS.md names slot_mapping: "per token, the KV slot it writes:
+ * block_id * block_size + offset"). Same in-place q/k results as svllm_qk_norm_rope_* /
+ * svllm_rope_*, and in the same pass, for every token t with slot s = slot_mapping[t]:
+ *   k_cache[s] = the rotated k[t]  ([num_kv_heads, head_dim]),  v_cache[s] = v[t].
+ * k_cache, v_cache: [num_slots, num_kv_heads, head_dim] contiguous (a [num_blocks, block_size,
+ * num_kv_heads, head_dim] cache with num_slots = num_blocks * block_size); v: [num_tokens,
+ * num_kv_heads, head_dim] at row stride v_row_stride (a view of a fused qkv tensor works);
+ * slot_mapping: [num_tokens] int64, 8-byte aligned. A negative slot skips the token (padding);
+ * a slot >= num_slots writes nothing and raises SVLLM_DEVERR_BAD_INDEX.
+ * New op: the next step of the path after RoPE (planned with the paged KV cache,
+ * docs/ROADMAP.md:24-25).
+ */
+int svllm_qk_norm_rope_cache_bf16(void* q, void* k, const void* v, const void* q_weight,
+                                  const void* k_weight, const void* positions, int pos_type,
+                                  const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                                  int64_t num_slots, int64_t num_tokens, int64_t num_heads,
+                                  int64_t num_kv_heads, int64_t head_dim, int64_t q_row_stride,
+                                  int64_t k_row_stride, int64_t v_row_stride, float eps,
+                                  const float* inv_freq, svllm_stream stream);
+int svllm_qk_norm_rope_cache_f32(float* q, float* k, const float* v, const float* q_weight,
+                                 const float* k_weight, const void* positions, int pos_type,
+                                 const int64_t* slot_mapping, float* k_cache, float* v_cache,
+                                 int64_t num_slots, int64_t num_tokens, int64_t num_heads,
+                                 int64_t num_kv_heads, int64_t head_dim, int64_t q_row_stride,
+                                 int64_t k_row_stride, int64_t v_row_stride, float eps,
+                                 const float* inv_freq, svllm_stream stream);
+int svllm_rope_cache_bf16(void* q, void* k, const void* v, const void* positions, int pos_type,
+                          const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                          int64_t num_slots, int64_t num_tokens, int64_t num_heads,
+                          int64_t num_kv_heads, int64_t head_dim, int64_t q_row_stride,
+                          int64_t k_row_stride, int64_t v_row_stride, const float* inv_freq,
+                          svllm_stream stream);
+int svllm_rope_cache_f32(float* q, float* k, const float* v, const void* positions, int pos_type,
+                         const int64_t* slot_mapping, float* k_cache, float* v_cache,
+                         int64_t num_slots, int64_t num_tokens, int64_t num_heads,
+                         int64_t num_kv_heads, int64_t head_dim, int64_t q_row_stride,
+                         int64_t k_row_stride, int64_t v_row_stride, const float* inv_freq,
+                         svllm_stream stream);
 
 /*
  * Host helper: the rotary inverse-frequency table, head_dim/2 fp32 values written to the HOST

@@ -46,6 +46,13 @@ PYBIND11_MODULE(svllm_ops, m) {
         py::arg("theta"), py::arg("rope_scaling") = std::nullopt);
   m.def("rope", &svllm::ops::rope, py::arg("q"), py::arg("k"), py::arg("positions"),
         py::arg("theta"), py::arg("rope_scaling") = std::nullopt);
+  m.def("qk_norm_rope_cache", &svllm::ops::qk_norm_rope_cache, py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("q_weight"), py::arg("k_weight"), py::arg("positions"),
+        py::arg("slot_mapping"), py::arg("k_cache"), py::arg("v_cache"), py::arg("eps"),
+        py::arg("theta"), py::arg("rope_scaling") = std::nullopt);
+  m.def("rope_cache", &svllm::ops::rope_cache, py::arg("q"), py::arg("k"), py::arg("v"),
+        py::arg("positions"), py::arg("slot_mapping"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("theta"), py::arg("rope_scaling") = std::nullopt);
   m.def("rope_inv_freq", &svllm::ops::rope_inv_freq, py::arg("theta"), py::arg("head_dim"),
         py::arg("rope_scaling") = std::nullopt);
   m.def("silu_and_mul", &svllm::ops::silu_and_mul, py::arg("gate"), py::arg("up"));

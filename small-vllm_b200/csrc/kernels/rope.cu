@@ -19,6 +19,12 @@
 //     product forms it, and cos/sin are the CUDA math library's accurate cosf/sinf (no fast
 //     approximations: their error would grow with the angle), the same functions torch's cos and
 //     sin kernels call, so on one GPU the result equals the torch composite bit for bit.
+//   * Cache variants (qk_norm_rope_cache / rope_cache): the same pass also writes the token's
+//     rotated k and its v into a paged KV cache at slot_mapping[t] (the reference's AGENTS.md
+//     "slot_mapping": block_id * block_size + offset, so the cache [num_blocks, block_size,
+//     num_kv_heads, head_dim] is addressed as [num_slots, num_kv_heads, head_dim]). v rides in
+//     the same stage as q and k and is copied from shared memory; a negative slot skips the
+//     token (padding), a slot past the cache raises SVLLM_DEVERR_BAD_INDEX and writes nothing.
 //   * Plain path for everything else: one warp per token, element loads, still on the GPU.
 #include <cuda_runtime.h>
 
@@ -52,6 +58,13 @@ struct RopeArgs {
   int interleave;  // token order (WarpUnits)
   float eps;
   int* err;
+  // cache variants
+  const void* v;
+  const int64_t* slots;
+  void* k_cache;  // [num_slots, num_kv_heads, head_dim]
+  void* v_cache;
+  int64_t v_stride;
+  int64_t num_slots;
   // bulk-copy path
   int stages;
   int stage_bytes;
@@ -131,7 +144,13 @@ struct LaneTrig<F32> {
   }
 };
 
-template <class E, int G, bool kNorm>
+// The cache slot of token t, or -1 for "write nothing" (a negative slot is padding; a slot past
+// the cache is an error, raised by the caller of this helper).
+__device__ __forceinline__ int64_t load_slot(const RopeArgs& a, int64_t t) {
+  return __ldg(reinterpret_cast<const long long*>(a.slots) + t);
+}
+
+template <class E, int G, bool kNorm, bool kCache>
 __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ RopeArgs a) {
   using S = typename E::Storage;
   constexpr int kVec = E::kPerVec;
@@ -148,6 +167,7 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
   const int total_heads = a.num_heads + a.num_kv_heads;
   const uint32_t q_bytes = static_cast<uint32_t>(num_heads) * kDim * sizeof(S);
   const uint32_t k_bytes = static_cast<uint32_t>(a.num_kv_heads) * kDim * sizeof(S);
+  const uint32_t v_bytes = kCache ? k_bytes : 0;  // one v row per token, same shape as k
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * a.stages;
   float* inv_sm = reinterpret_cast<float*>(smem + a.scratch_offset);
@@ -178,15 +198,20 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
   const int64_t n = wu.count;
   const int64_t q_stride_b = a.q_stride * static_cast<int64_t>(sizeof(S));
   const int64_t k_stride_b = a.k_stride * static_cast<int64_t>(sizeof(S));
+  const int64_t v_stride_b = a.v_stride * static_cast<int64_t>(sizeof(S));
 
   auto issue = [&](int64_t j) {
     const int s = static_cast<int>(j % a.stages);
     uint8_t* st = ring + static_cast<size_t>(s) * a.stage_bytes;
     const int64_t t = wu.at(j);
-    mbar_arrive_expect_tx(&bars[s], q_bytes + k_bytes);
+    mbar_arrive_expect_tx(&bars[s], q_bytes + k_bytes + v_bytes);
     if (q_bytes) bulk_load(st, static_cast<const uint8_t*>(a.q) + t * q_stride_b, q_bytes, &bars[s]);
     if (k_bytes) {
       bulk_load(st + q_bytes, static_cast<const uint8_t*>(a.k) + t * k_stride_b, k_bytes, &bars[s]);
+    }
+    if constexpr (kCache) {
+      bulk_load(st + q_bytes + k_bytes, static_cast<const uint8_t*>(a.v) + t * v_stride_b,
+                v_bytes, &bars[s]);
     }
   };
 
@@ -196,11 +221,21 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
 
   // Positions run one token ahead of use, so their load latency hides behind a token's work.
   float pos_next = n > 0 ? load_position(a.positions, a.pos_is_i64, wu.at(0)) : 0.0f;
+  int64_t slot_next = kCache && n > 0 ? load_slot(a, wu.at(0)) : -1;
 
   int64_t j = 0;
   for (; j < n; ++j) {
     const float pos = pos_next;
     if (j + 1 < n) pos_next = load_position(a.positions, a.pos_is_i64, wu.at(j + 1));
+    int64_t slot = -1;
+    if constexpr (kCache) {
+      slot = slot_next;
+      if (j + 1 < n) slot_next = load_slot(a, wu.at(j + 1));
+      if (slot >= a.num_slots) {
+        if (lane == 0) raise_error(a.err, kErrBadIndex);
+        slot = -1;
+      }
+    }
 
     // The token's (cos, sin) table, shared by every head.
     for (int i = lane; i < kHalf; i += kWarpSize) {
@@ -256,6 +291,23 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
                             static_cast<int64_t>(h - num_heads) * kDim;
         st_global_v4(dst + sub * kVec, lo);
         st_global_v4(dst + kHalf + sub * kVec, hi);
+        if constexpr (kCache) {
+          if (!is_q && slot >= 0) {
+            S* kc = static_cast<S*>(a.k_cache) + slot * a.num_kv_heads * kDim +
+                    static_cast<int64_t>(h - num_heads) * kDim;
+            st_global_v4(kc + sub * kVec, lo);
+            st_global_v4(kc + kHalf + sub * kVec, hi);
+          }
+        }
+      }
+    }
+    if constexpr (kCache) {
+      if (slot >= 0) {  // v goes to the cache as it is
+        const uint8_t* vs = st + q_bytes + k_bytes;
+        uint8_t* vc = static_cast<uint8_t*>(a.v_cache) + slot * static_cast<int64_t>(v_bytes);
+        for (uint32_t b = lane * 16; b < v_bytes; b += kWarpSize * 16) {
+          st_global_v4(vc + b, ld_shared_v4(vs + b));
+        }
       }
     }
     __syncwarp();
@@ -306,7 +358,7 @@ __device__ float reference_order_inv_rms(const typename E::Storage* x, int n, fl
 }
 
 // Plain path: one warp per token, any head_dim (even), any alignment.
-template <class E, bool kNorm>
+template <class E, bool kNorm, bool kCache>
 __global__ void __launch_bounds__(256) rope_plain_kernel(const __grid_constant__ RopeArgs a) {
   using S = typename E::Storage;
   const int lane = threadIdx.x % kWarpSize;
@@ -320,6 +372,14 @@ __global__ void __launch_bounds__(256) rope_plain_kernel(const __grid_constant__
                    threadIdx.x / kWarpSize;
        t < a.num_tokens; t += warps_total) {
     const float pos = load_position(a.positions, a.pos_is_i64, t);
+    int64_t slot = -1;
+    if constexpr (kCache) {
+      slot = load_slot(a, t);
+      if (slot >= a.num_slots) {
+        if (lane == 0) raise_error(a.err, kErrBadIndex);
+        slot = -1;
+      }
+    }
     for (int h = 0; h < total_heads; ++h) {
       const bool is_q = h < a.num_heads;
       S* x = is_q ? static_cast<S*>(a.q) + t * a.q_stride + static_cast<int64_t>(h) * dim
@@ -344,35 +404,62 @@ __global__ void __launch_bounds__(256) rope_plain_kernel(const __grid_constant__
         rotate_pairs<E>(lo, hi, c, s);
         x[i] = E::from_float(lo[0]);
         x[i + half] = E::from_float(hi[0]);
+        if constexpr (kCache) {
+          if (!is_q && slot >= 0) {
+            S* kc = static_cast<S*>(a.k_cache) + (slot * a.num_kv_heads + (h - a.num_heads)) * dim;
+            kc[i] = E::from_float(lo[0]);
+            kc[i + half] = E::from_float(hi[0]);
+          }
+        }
       }
       __syncwarp();
+    }
+    if constexpr (kCache) {
+      if (slot >= 0) {
+        const S* v = static_cast<const S*>(a.v) + t * a.v_stride;
+        S* vc = static_cast<S*>(a.v_cache) + slot * a.num_kv_heads * dim;
+        for (int i = lane; i < a.num_kv_heads * dim; i += kWarpSize) vc[i] = v[i];
+      }
     }
   }
 }
 
-template <class E, bool kNorm>
 using RopeKernel = void (*)(RopeArgs);
 
-template <class E, bool kNorm>
-RopeKernel<E, kNorm> pick_bulk_kernel(int head_dim) {
+template <class E, bool kNorm, bool kCache>
+RopeKernel pick_bulk_kernel(int head_dim) {
   constexpr int kVec = E::kPerVec;
   if (head_dim % (2 * kVec) != 0) return nullptr;
   switch (head_dim / (2 * kVec)) {
-    case 2: return rope_bulk_kernel<E, 2, kNorm>;
-    case 4: return rope_bulk_kernel<E, 4, kNorm>;
-    case 8: return rope_bulk_kernel<E, 8, kNorm>;
-    case 16: return rope_bulk_kernel<E, 16, kNorm>;
-    case 32: return rope_bulk_kernel<E, 32, kNorm>;
+    case 2: return rope_bulk_kernel<E, 2, kNorm, kCache>;
+    case 4: return rope_bulk_kernel<E, 4, kNorm, kCache>;
+    case 8: return rope_bulk_kernel<E, 8, kNorm, kCache>;
+    case 16: return rope_bulk_kernel<E, 16, kNorm, kCache>;
+    case 32: return rope_bulk_kernel<E, 32, kNorm, kCache>;
     default: return nullptr;
   }
 }
 
-template <class E, bool kNorm>
+// The paged-KV destination of the cache variants (all null / zero without one).
+struct CacheTarget {
+  const void* v = nullptr;
+  const int64_t* slots = nullptr;
+  void* k_cache = nullptr;
+  void* v_cache = nullptr;
+  int64_t v_stride = 0;
+  int64_t num_slots = 0;
+};
+
+template <class E, bool kNorm, bool kCache>
 int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
                 const void* positions, int pos_type, int64_t num_tokens, int64_t num_heads,
                 int64_t num_kv_heads, int64_t head_dim, int64_t q_stride, int64_t k_stride,
-                float eps, const float* inv_freq, cudaStream_t stream) {
+                float eps, const float* inv_freq, const CacheTarget& cache, cudaStream_t stream) {
   using S = typename E::Storage;
+  if (kCache && (num_kv_heads <= 0 || cache.num_slots < 0 ||
+                 cache.v_stride < num_kv_heads * head_dim)) {
+    return SVLLM_ERR_INVALID_ARGUMENT;
+  }
   if (num_tokens < 0 || num_heads < 0 || num_kv_heads < 0 || head_dim <= 0 || head_dim % 2 != 0 ||
       head_dim > 2 * kMaxHalfDim || (pos_type != SVLLM_INDEX_I32 && pos_type != SVLLM_INDEX_I64) ||
       (num_heads > 0 && q_stride < num_heads * head_dim) ||
@@ -384,6 +471,13 @@ int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
       (num_kv_heads > 0 && k == nullptr) ||
       (kNorm && ((num_heads > 0 && q_weight == nullptr) ||
                  (num_kv_heads > 0 && k_weight == nullptr)))) {
+    return SVLLM_ERR_INVALID_ARGUMENT;
+  }
+  if (kCache && (cache.v == nullptr || cache.slots == nullptr || cache.k_cache == nullptr ||
+                 cache.v_cache == nullptr)) {
+    return SVLLM_ERR_INVALID_ARGUMENT;
+  }
+  if (kCache && (reinterpret_cast<uintptr_t>(cache.slots) & 7u) != 0) {
     return SVLLM_ERR_INVALID_ARGUMENT;
   }
   if (num_heads + num_kv_heads > (1 << 16)) return SVLLM_ERR_TOO_LARGE;
@@ -411,6 +505,12 @@ int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
   a.interleave = 1;  // measured faster than contiguous shares on B200
   a.eps = eps;
   a.err = err;
+  a.v = cache.v;
+  a.slots = cache.slots;
+  a.k_cache = cache.k_cache;
+  a.v_cache = cache.v_cache;
+  a.v_stride = cache.v_stride;
+  a.num_slots = cache.num_slots;
   std::memcpy(a.inv_freq, inv_freq, sizeof(float) * (head_dim / 2));
   a.norm_vec = sizeof(S) == 2 && head_dim % 8 == 0 && aligned16(q) && aligned16(k) &&
                (q_stride * sizeof(S)) % 16 == 0 && (k_stride * sizeof(S)) % 16 == 0 &&
@@ -419,14 +519,18 @@ int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
   const int64_t head_bytes = head_dim * static_cast<int64_t>(sizeof(S));
   const int64_t q_bytes = num_heads * head_bytes;
   const int64_t k_bytes = num_kv_heads * head_bytes;
+  const int64_t v_bytes = kCache ? k_bytes : 0;
   const bool bulk_ok =
       (num_heads == 0 || (aligned16(q) && (q_stride * sizeof(S)) % 16 == 0)) &&
       (num_kv_heads == 0 || (aligned16(k) && (k_stride * sizeof(S)) % 16 == 0)) &&
-      (!kNorm || (aligned16(a.q_weight) && aligned16(a.k_weight)));
-  const RopeKernel<E, kNorm> kernel = bulk_ok ? pick_bulk_kernel<E, kNorm>(static_cast<int>(head_dim)) : nullptr;
+      (!kNorm || (aligned16(a.q_weight) && aligned16(a.k_weight))) &&
+      (!kCache || (aligned16(cache.v) && (cache.v_stride * sizeof(S)) % 16 == 0 &&
+                   aligned16(cache.k_cache) && aligned16(cache.v_cache)));
+  const RopeKernel kernel =
+      bulk_ok ? pick_bulk_kernel<E, kNorm, kCache>(static_cast<int>(head_dim)) : nullptr;
   if (kernel != nullptr) {
     const PipelineShape shape = pipeline_shape(kNorm ? OpId::kQkNormRope : OpId::kRope);
-    a.stage_bytes = static_cast<int>(round_up(q_bytes + k_bytes, 128));
+    a.stage_bytes = static_cast<int>(round_up(q_bytes + k_bytes + v_bytes, 128));
     int warps = warps_for(num_tokens, shape.warps, device);
     int stages = shape.stages;
     const int64_t half = head_dim / 2;
@@ -438,7 +542,7 @@ int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
     while (smem_for(warps, stages) > static_cast<int64_t>(kMaxSmemPerCta) && stages > 2) --stages;
     while (smem_for(warps, stages) > static_cast<int64_t>(kMaxSmemPerCta) && warps > 1) --warps;
     if (smem_for(warps, stages) <= static_cast<int64_t>(kMaxSmemPerCta) &&
-        q_bytes + k_bytes < (1 << 20)) {
+        q_bytes + k_bytes + v_bytes < (1 << 20)) {
       a.stages = stages;
       a.scratch_offset = static_cast<int>(round_up(static_cast<int64_t>(warps) * stages * 8, 128));
       a.ring_offset = a.scratch_offset +
@@ -455,7 +559,7 @@ int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
   }
 
   const int64_t grid = persistent_grid((num_tokens + 7) / 8, device, 8);
-  rope_plain_kernel<E, kNorm><<<static_cast<unsigned>(grid), 256, 0, stream>>>(a);
+  rope_plain_kernel<E, kNorm, kCache><<<static_cast<unsigned>(grid), 256, 0, stream>>>(a);
   return launch_status();
 }
 
@@ -473,9 +577,10 @@ int svllm_qk_norm_rope_bf16(void* q, void* k, const void* q_weight, const void* 
                             int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
                             int64_t q_row_stride, int64_t k_row_stride, float eps,
                             const float* inv_freq, svllm_stream stream) {
-  return launch_rope<Bf16, true>(q, k, q_weight, k_weight, positions, pos_type, num_tokens,
-                                 num_heads, num_kv_heads, head_dim, q_row_stride, k_row_stride,
-                                 eps, inv_freq, reinterpret_cast<cudaStream_t>(stream));
+  return launch_rope<Bf16, true, false>(q, k, q_weight, k_weight, positions, pos_type,
+                                        num_tokens, num_heads, num_kv_heads, head_dim,
+                                        q_row_stride, k_row_stride, eps, inv_freq, {},
+                                        reinterpret_cast<cudaStream_t>(stream));
 }
 
 int svllm_qk_norm_rope_f32(float* q, float* k, const float* q_weight, const float* k_weight,
@@ -483,27 +588,100 @@ int svllm_qk_norm_rope_f32(float* q, float* k, const float* q_weight, const floa
                            int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
                            int64_t q_row_stride, int64_t k_row_stride, float eps,
                            const float* inv_freq, svllm_stream stream) {
-  return launch_rope<F32, true>(q, k, q_weight, k_weight, positions, pos_type, num_tokens,
-                                num_heads, num_kv_heads, head_dim, q_row_stride, k_row_stride,
-                                eps, inv_freq, reinterpret_cast<cudaStream_t>(stream));
+  return launch_rope<F32, true, false>(q, k, q_weight, k_weight, positions, pos_type,
+                                       num_tokens, num_heads, num_kv_heads, head_dim,
+                                       q_row_stride, k_row_stride, eps, inv_freq, {},
+                                       reinterpret_cast<cudaStream_t>(stream));
 }
 
 int svllm_rope_bf16(void* q, void* k, const void* positions, int pos_type, int64_t num_tokens,
                     int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
                     int64_t q_row_stride, int64_t k_row_stride, const float* inv_freq,
                     svllm_stream stream) {
-  return launch_rope<Bf16, false>(q, k, nullptr, nullptr, positions, pos_type, num_tokens,
-                                  num_heads, num_kv_heads, head_dim, q_row_stride, k_row_stride,
-                                  0.0f, inv_freq, reinterpret_cast<cudaStream_t>(stream));
+  return launch_rope<Bf16, false, false>(q, k, nullptr, nullptr, positions, pos_type,
+                                         num_tokens, num_heads, num_kv_heads, head_dim,
+                                         q_row_stride, k_row_stride, 0.0f, inv_freq, {},
+                                         reinterpret_cast<cudaStream_t>(stream));
 }
 
 int svllm_rope_f32(float* q, float* k, const void* positions, int pos_type, int64_t num_tokens,
                    int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
                    int64_t q_row_stride, int64_t k_row_stride, const float* inv_freq,
                    svllm_stream stream) {
-  return launch_rope<F32, false>(q, k, nullptr, nullptr, positions, pos_type, num_tokens,
-                                 num_heads, num_kv_heads, head_dim, q_row_stride, k_row_stride,
-                                 0.0f, inv_freq, reinterpret_cast<cudaStream_t>(stream));
+  return launch_rope<F32, false, false>(q, k, nullptr, nullptr, positions, pos_type,
+                                        num_tokens, num_heads, num_kv_heads, head_dim,
+                                        q_row_stride, k_row_stride, 0.0f, inv_freq, {},
+                                        reinterpret_cast<cudaStream_t>(stream));
+}
+
+namespace {
+
+svllm::k::CacheTarget cache_target(const void* v, const int64_t* slot_mapping, void* k_cache,
+                                   void* v_cache, int64_t num_slots, int64_t v_row_stride) {
+  svllm::k::CacheTarget c;
+  c.v = v;
+  c.slots = slot_mapping;
+  c.k_cache = k_cache;
+  c.v_cache = v_cache;
+  c.num_slots = num_slots;
+  c.v_stride = v_row_stride;
+  return c;
+}
+
+}  // namespace
+
+int svllm_qk_norm_rope_cache_bf16(void* q, void* k, const void* v, const void* q_weight,
+                                  const void* k_weight, const void* positions, int pos_type,
+                                  const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                                  int64_t num_slots, int64_t num_tokens, int64_t num_heads,
+                                  int64_t num_kv_heads, int64_t head_dim, int64_t q_row_stride,
+                                  int64_t k_row_stride, int64_t v_row_stride, float eps,
+                                  const float* inv_freq, svllm_stream stream) {
+  return launch_rope<Bf16, true, true>(
+      q, k, q_weight, k_weight, positions, pos_type, num_tokens, num_heads, num_kv_heads,
+      head_dim, q_row_stride, k_row_stride, eps, inv_freq,
+      cache_target(v, slot_mapping, k_cache, v_cache, num_slots, v_row_stride),
+      reinterpret_cast<cudaStream_t>(stream));
+}
+
+int svllm_qk_norm_rope_cache_f32(float* q, float* k, const float* v, const float* q_weight,
+                                 const float* k_weight, const void* positions, int pos_type,
+                                 const int64_t* slot_mapping, float* k_cache, float* v_cache,
+                                 int64_t num_slots, int64_t num_tokens, int64_t num_heads,
+                                 int64_t num_kv_heads, int64_t head_dim, int64_t q_row_stride,
+                                 int64_t k_row_stride, int64_t v_row_stride, float eps,
+                                 const float* inv_freq, svllm_stream stream) {
+  return launch_rope<F32, true, true>(
+      q, k, q_weight, k_weight, positions, pos_type, num_tokens, num_heads, num_kv_heads,
+      head_dim, q_row_stride, k_row_stride, eps, inv_freq,
+      cache_target(v, slot_mapping, k_cache, v_cache, num_slots, v_row_stride),
+      reinterpret_cast<cudaStream_t>(stream));
+}
+
+int svllm_rope_cache_bf16(void* q, void* k, const void* v, const void* positions, int pos_type,
+                          const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                          int64_t num_slots, int64_t num_tokens, int64_t num_heads,
+                          int64_t num_kv_heads, int64_t head_dim, int64_t q_row_stride,
+                          int64_t k_row_stride, int64_t v_row_stride, const float* inv_freq,
+                          svllm_stream stream) {
+  return launch_rope<Bf16, false, true>(
+      q, k, nullptr, nullptr, positions, pos_type, num_tokens, num_heads, num_kv_heads, head_dim,
+      q_row_stride, k_row_stride, 0.0f, inv_freq,
+      cache_target(v, slot_mapping, k_cache, v_cache, num_slots, v_row_stride),
+      reinterpret_cast<cudaStream_t>(stream));
+}
+
+int svllm_rope_cache_f32(float* q, float* k, const float* v, const void* positions, int pos_type,
+                         const int64_t* slot_mapping, float* k_cache, float* v_cache,
+                         int64_t num_slots, int64_t num_tokens, int64_t num_heads,
+                         int64_t num_kv_heads, int64_t head_dim, int64_t q_row_stride,
+                         int64_t k_row_stride, int64_t v_row_stride, const float* inv_freq,
+                         svllm_stream stream) {
+  return launch_rope<F32, false, true>(
+      q, k, nullptr, nullptr, positions, pos_type, num_tokens, num_heads, num_kv_heads, head_dim,
+      q_row_stride, k_row_stride, 0.0f, inv_freq,
+      cache_target(v, slot_mapping, k_cache, v_cache, num_slots, v_row_stride),
+      reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -2,6 +2,7 @@
 #include <ATen/Parallel.h>
 #include <c10/util/BFloat16.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <vector>
@@ -81,6 +82,30 @@ void rope(const at::Tensor& q, const at::Tensor& k, const at::Tensor& q_weight,
       }
     }
   });
+}
+
+int64_t write_kv_cache(const at::Tensor& k, const at::Tensor& v, const at::Tensor& slot_mapping,
+                       const at::Tensor& k_cache, const at::Tensor& v_cache) {
+  const int64_t num_tokens = k.size(0);
+  const int64_t row = k.size(1) * k.size(2);  // elements of one slot
+  const int64_t num_slots = k_cache.size(0);
+  const auto* slots = slot_mapping.const_data_ptr<int64_t>();
+  const auto* kp = k.const_data_ptr<at::BFloat16>();
+  const auto* vp = v.const_data_ptr<at::BFloat16>();
+  auto* kc = k_cache.mutable_data_ptr<at::BFloat16>();
+  auto* vc = v_cache.mutable_data_ptr<at::BFloat16>();
+  int64_t bad = 0;
+  for (int64_t t = 0; t < num_tokens; ++t) {
+    const int64_t s = slots[t];
+    if (s < 0) continue;
+    if (s >= num_slots) {
+      ++bad;
+      continue;
+    }
+    std::copy(kp + t * k.stride(0), kp + t * k.stride(0) + row, kc + s * row);
+    std::copy(vp + t * v.stride(0), vp + t * v.stride(0) + row, vc + s * row);
+  }
+  return bad;
 }
 
 }  // namespace svllm::ops::cpu_impl

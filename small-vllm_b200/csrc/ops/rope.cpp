@@ -59,10 +59,19 @@ at::Tensor token_view(const char* op, const char* name, const at::Tensor& t) {
   return t.view({-1, heads, head_dim});
 }
 
+// Cache-write operands of the *_cache ops (all undefined for plain rope / qk_norm_rope).
+struct KvCacheArgs {
+  at::Tensor v;
+  at::Tensor slot_mapping;
+  at::Tensor k_cache;
+  at::Tensor v_cache;
+};
+
 void check_and_run(const char* op, const at::Tensor& q, const at::Tensor& k,
                    const at::Tensor& q_weight, const at::Tensor& k_weight,
                    const at::Tensor& positions, double eps, double theta,
-                   const std::optional<Llama3RopeScaling>& rope_scaling) {
+                   const std::optional<Llama3RopeScaling>& rope_scaling,
+                   const KvCacheArgs& cache = {}) {
   const bool norm = q_weight.defined();
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 &&
                   (!norm || (q_weight.scalar_type() == at::kBFloat16 &&
@@ -96,14 +105,58 @@ void check_and_run(const char* op, const at::Tensor& q, const at::Tensor& k,
               norm ? " or the weights are" : " are", " elsewhere (k on ", k.device(),
               ", positions on ", positions.device(), ")");
 
+  const bool with_cache = cache.v.defined();
+  at::Tensor v3, kc, vc;
+  if (with_cache) {
+    TORCH_CHECK(cache.v.scalar_type() == q.scalar_type() &&
+                    cache.k_cache.scalar_type() == q.scalar_type() &&
+                    cache.v_cache.scalar_type() == q.scalar_type(),
+                op, ": expected bf16 v, k_cache and v_cache");
+    v3 = token_view(op, "v", cache.v);
+    TORCH_CHECK(v3.sizes() == k3.sizes(), op, ": v of shape ", cache.v.sizes(),
+                " does not match k of shape ", k.sizes());
+    const int64_t kv_heads = k3.size(1);
+    for (const at::Tensor* c : {&cache.k_cache, &cache.v_cache}) {
+      TORCH_CHECK(c->dim() >= 2 && c->size(-1) == head_dim && c->size(-2) == kv_heads &&
+                      c->is_contiguous(),
+                  op, ": caches must be contiguous [..., num_kv_heads, head_dim] = [..., ",
+                  kv_heads, ", ", head_dim, "], got shape ", c->sizes());
+    }
+    TORCH_CHECK(cache.k_cache.sizes() == cache.v_cache.sizes(), op, ": k_cache of shape ",
+                cache.k_cache.sizes(), " does not match v_cache of shape ",
+                cache.v_cache.sizes());
+    TORCH_CHECK(cache.slot_mapping.scalar_type() == at::kLong &&
+                    cache.slot_mapping.is_contiguous() &&
+                    cache.slot_mapping.numel() == q3.size(0),
+                op, ": slot_mapping must be contiguous int64 with one slot per token");
+    const bool cache_same_device = cache.v.device() == q.device() &&
+                                   cache.slot_mapping.device() == q.device() &&
+                                   cache.k_cache.device() == q.device() &&
+                                   cache.v_cache.device() == q.device();
+    TORCH_CHECK(cache_same_device, op, ": q is on ", q.device(),
+                " but v, slot_mapping or a cache is elsewhere");
+    kc = cache.k_cache.view({-1, kv_heads, head_dim});
+    vc = cache.v_cache.view({-1, kv_heads, head_dim});
+  }
+
   const std::vector<float>& inv_freq = cached_inv_freq(theta, head_dim, rope_scaling);
 
   switch (q.device().type()) {
-    case c10::DeviceType::CPU:
+    case c10::DeviceType::CPU: {
       cpu_impl::rope(q3, k3, q_weight, k_weight, positions, eps, inv_freq.data());
+      if (with_cache) {
+        const int64_t bad = cpu_impl::write_kv_cache(k3, v3, cache.slot_mapping, kc, vc);
+        TORCH_CHECK(bad == 0, op, ": ", bad, " slots past the cache's ", kc.size(0));
+      }
       break;
+    }
     case c10::DeviceType::CUDA:
-      cuda_impl::rope(q3, k3, q_weight, k_weight, positions, eps, inv_freq.data());
+      if (with_cache) {
+        cuda_impl::rope_cache(q3, k3, v3, q_weight, k_weight, positions, cache.slot_mapping, kc,
+                              vc, eps, inv_freq.data());
+      } else {
+        cuda_impl::rope(q3, k3, q_weight, k_weight, positions, eps, inv_freq.data());
+      }
       break;
     default:
       TORCH_CHECK(false, op, ": unsupported device ", q.device());
@@ -160,6 +213,25 @@ void qk_norm_rope(const at::Tensor& q, const at::Tensor& k, const at::Tensor& q_
   TORCH_CHECK(q_weight.defined() && k_weight.defined(),
               "qk_norm_rope: q_weight and k_weight are required");
   check_and_run("qk_norm_rope", q, k, q_weight, k_weight, positions, eps, theta, rope_scaling);
+}
+
+void qk_norm_rope_cache(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                        const at::Tensor& q_weight, const at::Tensor& k_weight,
+                        const at::Tensor& positions, const at::Tensor& slot_mapping,
+                        const at::Tensor& k_cache, const at::Tensor& v_cache, double eps,
+                        double theta, const std::optional<Llama3RopeScaling>& rope_scaling) {
+  TORCH_CHECK(q_weight.defined() && k_weight.defined(),
+              "qk_norm_rope_cache: q_weight and k_weight are required");
+  check_and_run("qk_norm_rope_cache", q, k, q_weight, k_weight, positions, eps, theta,
+                rope_scaling, {v, slot_mapping, k_cache, v_cache});
+}
+
+void rope_cache(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                const at::Tensor& positions, const at::Tensor& slot_mapping,
+                const at::Tensor& k_cache, const at::Tensor& v_cache, double theta,
+                const std::optional<Llama3RopeScaling>& rope_scaling) {
+  check_and_run("rope_cache", q, k, at::Tensor(), at::Tensor(), positions, 0.0, theta,
+                rope_scaling, {v, slot_mapping, k_cache, v_cache});
 }
 
 }  // namespace svllm::ops

@@ -38,6 +38,30 @@ void qk_norm_rope(const at::Tensor& q, const at::Tensor& k, const at::Tensor& q_
                   const at::Tensor& k_weight, const at::Tensor& positions, double eps,
                   double theta, const std::optional<Llama3RopeScaling>& rope_scaling);
 
+// Definition: qk_norm_rope (Qwen3) or rope (Llama, when q_weight is undefined) fused with the
+//             paged-KV cache write that follows it in a decoder layer.
+// Formula:    q and k as qk_norm_rope / rope; then for every token t with s = slot_mapping[t]
+//             >= 0: k_cache[s] = the rotated k[t], v_cache[s] = v[t] (the reference's
+//             slot_mapping: block_id * block_size + offset, AGENTS.md "Names").
+// Domain:     As rope(); v like k ([num_tokens, num_kv_heads, head_dim], tokens at any stride);
+//             k_cache and v_cache contiguous [..., num_kv_heads, head_dim] of the same dtype
+//             (e.g. [num_blocks, block_size, num_kv_heads, head_dim]); slot_mapping
+//             [num_tokens] int64, contiguous; one device.
+// Returns:    Nothing; q, k, and the cache slots hold the results. A negative slot skips its
+//             token (padding).
+// Throws:     As rope(), or on cache shape / dtype mismatches. A slot past the cache throws on
+//             CPU; on CUDA it writes nothing and raises a bit of the device error word.
+void qk_norm_rope_cache(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                        const at::Tensor& q_weight, const at::Tensor& k_weight,
+                        const at::Tensor& positions, const at::Tensor& slot_mapping,
+                        const at::Tensor& k_cache, const at::Tensor& v_cache, double eps,
+                        double theta, const std::optional<Llama3RopeScaling>& rope_scaling);
+
+void rope_cache(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                const at::Tensor& positions, const at::Tensor& slot_mapping,
+                const at::Tensor& k_cache, const at::Tensor& v_cache, double theta,
+                const std::optional<Llama3RopeScaling>& rope_scaling);
+
 // Definition: The inverse-frequency table rope() uses, computed on the CPU with torch's own fp32
 //             ops in Hugging Face's order (_compute_default_rope_parameters, and
 //             _compute_llama3_parameters when rope_scaling is given), so it equals Hugging Face's

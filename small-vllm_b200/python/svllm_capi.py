@@ -50,6 +50,14 @@ SIGNATURES = {
     "svllm_rope_bf16": [_P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P],
     "svllm_rope_f32": [_P, _P, _P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P],
     "svllm_rope_inv_freq": [ctypes.c_double, _I64, _P, _P],
+    "svllm_qk_norm_rope_cache_bf16": [_P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _I64, _I64, _I64,
+                                      _I64, _I64, _I64, _I64, _I64, _F, _P, _P],
+    "svllm_qk_norm_rope_cache_f32": [_P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _I64, _I64, _I64,
+                                     _I64, _I64, _I64, _I64, _I64, _F, _P, _P],
+    "svllm_rope_cache_bf16": [_P, _P, _P, _P, _I, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
+                              _I64, _I64, _P, _P],
+    "svllm_rope_cache_f32": [_P, _P, _P, _P, _I, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
+                             _I64, _I64, _P, _P],
     "svllm_silu_and_mul_bf16": [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
     "svllm_silu_and_mul_f32": [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
     "svllm_embedding_bf16": [_P, _P, _I, _P, _I64, _I64, _I64, _I64, _I64, _P, _P],
@@ -167,6 +175,31 @@ def rope(q, k, positions, inv, stream=None) -> None:
     check(fn(q.data_ptr(), k.data_ptr(), positions.data_ptr(), _index_type(positions),
              q.shape[0], q.shape[1], k.shape[1], q.shape[2], q.stride(0), k.stride(0),
              ctypes.cast(arr, _P), _stream(stream)), "rope")
+
+
+def qk_norm_rope_cache(q, k, v, q_weight, k_weight, positions, slot_mapping, k_cache, v_cache,
+                       eps: float, inv, stream=None) -> None:
+    """qk_norm_rope plus the paged-KV write; caches are [num_slots, Hk, D] (or a
+    [blocks, block_size, Hk, D] tensor, flattened)."""
+    arr = _inv_array(inv)
+    num_slots = k_cache.numel() // (k.shape[1] * k.shape[2])
+    fn = getattr(lib(), f"svllm_qk_norm_rope_cache_{_bf16_or_f32(q)}")
+    check(fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), q_weight.data_ptr(), k_weight.data_ptr(),
+             positions.data_ptr(), _index_type(positions), slot_mapping.data_ptr(),
+             k_cache.data_ptr(), v_cache.data_ptr(), num_slots, q.shape[0], q.shape[1],
+             k.shape[1], q.shape[2], q.stride(0), k.stride(0), v.stride(0), eps,
+             ctypes.cast(arr, _P), _stream(stream)), "qk_norm_rope_cache")
+
+
+def rope_cache(q, k, v, positions, slot_mapping, k_cache, v_cache, inv, stream=None) -> None:
+    arr = _inv_array(inv)
+    num_slots = k_cache.numel() // (k.shape[1] * k.shape[2])
+    fn = getattr(lib(), f"svllm_rope_cache_{_bf16_or_f32(q)}")
+    check(fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), positions.data_ptr(),
+             _index_type(positions), slot_mapping.data_ptr(), k_cache.data_ptr(),
+             v_cache.data_ptr(), num_slots, q.shape[0], q.shape[1], k.shape[1], q.shape[2],
+             q.stride(0), k.stride(0), v.stride(0), ctypes.cast(arr, _P), _stream(stream)),
+          "rope_cache")
 
 
 def silu_and_mul(out, gate, up, stream=None) -> None:

@@ -345,3 +345,105 @@ def test_silu_table_path_is_exhaustively_identical(cuda):
     bits = lambda t: t.view(torch.int16)  # noqa: E731  (NaN == NaN as bit patterns)
     assert torch.equal(bits(out[:1]), bits(small)), "table path != direct path"
     assert torch.equal(bits(out), bits(expect)), "table path != torch silu * up"
+
+
+# ---------------------------------------------------------------------------------------------
+# rotary + paged-KV cache write, through the C ABI
+
+@pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
+@pytest.mark.parametrize("with_norm, hq, hk, d", [(True, 16, 8, 128), (False, 32, 8, 64),
+                                                  (True, 4, 2, 96)], ids=str)
+def test_rope_cache(cuda, dt, with_norm, hq, hk, d):
+    T, block_size = 1500, 16
+    num_blocks = (T + block_size - 1) // block_size + 5
+    qkv = random_t(T, (hq + 2 * hk) * d, dtype=dt, device=cuda, seed=40)
+    q = qkv[:, : hq * d].view(T, hq, d)
+    k = qkv[:, hq * d:(hq + hk) * d].view(T, hk, d)
+    v = qkv[:, (hq + hk) * d:].view(T, hk, d)
+    qw = random_t(d, dtype=dt, device=cuda, seed=41, scale=0.1, shift=1.0)
+    kw = random_t(d, dtype=dt, device=cuda, seed=42, scale=0.1, shift=1.0)
+    pos = _positions(T, 32768, torch.int64, cuda, 43)
+    g = torch.Generator().manual_seed(44)
+    perm = torch.randperm(num_blocks, generator=g)
+    t = torch.arange(T)
+    slots = (perm[t // block_size] * block_size + t % block_size)
+    slots[::11] = -1
+    slots = slots.to(cuda)
+    k_cache = torch.zeros(num_blocks, block_size, hk, d, dtype=dt, device=cuda)
+    v_cache = torch.zeros_like(k_cache)
+    inv = oracle.inv_freq(1e6, d)
+    qn, kn = np_of(q.contiguous()), np_of(k.contiguous())
+    if with_norm:
+        rq, rk = oracle.qk_norm_rope(qn, kn, np_of(qw), np_of(kw), np_of(pos), 1e-6, inv)
+    else:
+        rq, rk = oracle.rope(qn, kn, np_of(pos), inv)
+    v_before = v.clone()
+    if with_norm:
+        capi.qk_norm_rope_cache(q, k, v, qw, kw, pos, slots, k_cache, v_cache, 1e-6, inv)
+    else:
+        capi.rope_cache(q, k, v, pos, slots, k_cache, v_cache, inv)
+    torch.cuda.synchronize()
+    written = slots >= 0
+    flat_k = k_cache.view(-1, hk, d)
+    flat_v = v_cache.view(-1, hk, d)
+    s_w = slots[written]
+    # the cache rows are exactly the kernel's own rotated k and the untouched v
+    assert torch.equal(flat_k[s_w], k[written])
+    assert torch.equal(flat_v[s_w], v_before[written])
+    mask = torch.ones(flat_k.shape[0], dtype=torch.bool, device=cuda)
+    mask[s_w] = False
+    assert not flat_k[mask].any() and not flat_v[mask].any(), "a slot not in slot_mapping changed"
+    if dt == torch.bfloat16:
+        assert (np_of(q.contiguous()) == rq).mean() > 0.99
+        assert (np_of(k.contiguous()) == rk).mean() > 0.99
+    else:
+        half = d // 2
+
+        def pair(x):
+            p = np.abs(np.asarray(x, dtype=np.float64))
+            m = p[..., :half] + p[..., half:]
+            return np.concatenate([m, m], axis=-1)
+
+        pre_q = oracle.rms_norm(qn.reshape(-1, d), np_of(qw), 1e-6).reshape(qn.shape) \
+            if with_norm else qn
+        assert_rel_f32(q.contiguous(), rq, 1e-5, "q", scale=pair(pre_q))
+
+
+def test_rope_cache_matches_rope_then_copy(cuda):
+    """The fused op equals qk_norm_rope followed by a scatter of k and v into the cache."""
+    T, hq, hk, d = 777, 16, 8, 128
+    base = random_t(T, (hq + 2 * hk) * d, device=cuda, seed=45)
+    qw = random_t(d, device=cuda, seed=46, scale=0.1, shift=1.0)
+    kw = random_t(d, device=cuda, seed=47, scale=0.1, shift=1.0)
+    pos = _positions(T, 4096, torch.int32, cuda, 48)
+    slots = torch.randperm(T + 100, device=cuda)[:T]
+    inv = oracle.inv_freq(1e6, d)
+
+    def split(t):
+        return (t[:, : hq * d].view(T, hq, d), t[:, hq * d:(hq + hk) * d].view(T, hk, d),
+                t[:, (hq + hk) * d:].view(T, hk, d))
+
+    a, b = base.clone(), base.clone()
+    qa, ka, va = split(a)
+    qb, kb, vb = split(b)
+    kc = torch.zeros(T + 100, hk, d, dtype=torch.bfloat16, device=cuda)
+    vc = torch.zeros_like(kc)
+    capi.qk_norm_rope_cache(qa, ka, va, qw, kw, pos, slots, kc, vc, 1e-6, inv)
+    capi.qk_norm_rope(qb, kb, qw, kw, pos, 1e-6, inv)
+    kc2, vc2 = torch.zeros_like(kc), torch.zeros_like(vc)
+    kc2[slots], vc2[slots] = kb, vb
+    assert torch.equal(a, b) and torch.equal(kc, kc2) and torch.equal(vc, vc2)
+
+
+def test_rope_cache_slot_past_the_cache(cuda):
+    T, hk, d = 4, 2, 64
+    q = random_t(T, 4, d, device=cuda, seed=49)
+    k = random_t(T, hk, d, device=cuda, seed=50)
+    v = random_t(T, hk, d, device=cuda, seed=51)
+    kc = torch.zeros(8, hk, d, dtype=torch.bfloat16, device=cuda)
+    vc = torch.zeros_like(kc)
+    slots = torch.tensor([0, 8, 3, 100], device=cuda)
+    capi.rope_cache(q, k, v, torch.arange(T, device=cuda), slots, kc, vc, oracle.inv_freq(1e4, d))
+    assert capi.read_device_error(0, reset=True) & capi.DEVERR_BAD_INDEX
+    assert torch.equal(kc[0], k[0]) and torch.equal(vc[3], v[2])
+    assert not kc[[1, 2, 4, 5, 6, 7]].any()

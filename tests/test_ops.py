@@ -199,3 +199,64 @@ def test_embedding_rejects_bad_inputs():
         svllm_ops.embedding(torch.tensor([1]), table.float())
     with pytest.raises(RuntimeError, match="vocab, hidden"):
         svllm_ops.embedding(torch.tensor([1]), torch.ones(16, dtype=torch.bfloat16))
+
+
+# ---------------------------------------------------------------------------------------------
+# rotary + paged-KV cache write
+
+def _paged_slots(T, num_blocks, block_size, device, seed):
+    """Tokens laid out block by block over a random permutation of cache blocks, a few padded."""
+    g = torch.Generator().manual_seed(seed)
+    blocks = torch.randperm(num_blocks, generator=g)[: (T + block_size - 1) // block_size]
+    t = torch.arange(T)
+    slots = blocks[t // block_size] * block_size + t % block_size
+    slots[::7] = -1  # padding tokens write nothing
+    return slots.to(device)
+
+
+@pytest.mark.parametrize("with_norm", [True, False], ids=["qk_norm_rope_cache", "rope_cache"])
+def test_rope_cache(device, with_norm):
+    T, hq, hk, d, blocks, bs = 37, 16, 8, 128, 20, 16
+    qkv = random_bf16(T, (hq + 2 * hk) * d, device=device, seed=20)
+    q = qkv[:, : hq * d].view(T, hq, d)
+    k = qkv[:, hq * d:(hq + hk) * d].view(T, hk, d)
+    v = qkv[:, (hq + hk) * d:].view(T, hk, d)
+    qw = random_t(d, device=device, seed=21, scale=0.1, shift=1.0)
+    kw = random_t(d, device=device, seed=22, scale=0.1, shift=1.0)
+    pos = torch.arange(T, device=device) * 3
+    slots = _paged_slots(T, blocks, bs, device, seed=23)
+    k_cache = torch.full((blocks, bs, hk, d), 5.0, dtype=torch.bfloat16, device=device)
+    v_cache = torch.full((blocks, bs, hk, d), 7.0, dtype=torch.bfloat16, device=device)
+    inv = svllm_ops.rope_inv_freq(1e6, d)
+    if with_norm:
+        eq = hf_rope(hf_rms_norm(q, qw, QWEN_EPS), pos, inv)
+        ek = hf_rope(hf_rms_norm(k, kw, QWEN_EPS), pos, inv)
+    else:
+        eq, ek = hf_rope(q.clone(), pos, inv), hf_rope(k.clone(), pos, inv)
+    ev = v.clone()
+    if with_norm:
+        svllm_ops.qk_norm_rope_cache(q, k, v, qw, kw, pos, slots, k_cache, v_cache, QWEN_EPS, 1e6)
+    else:
+        svllm_ops.rope_cache(q, k, v, pos, slots, k_cache, v_cache, 1e6)
+    assert_close_bf16(q, eq, atol=2e-2)
+    assert_close_bf16(k, ek, atol=2e-2)
+    flat_k, flat_v = k_cache.view(-1, hk, d), v_cache.view(-1, hk, d)
+    written = slots >= 0
+    assert torch.equal(flat_k[slots[written]], k[written]), "cache holds the rotated k"
+    assert torch.equal(flat_v[slots[written]], ev[written]), "cache holds v"
+    untouched = torch.ones(blocks * bs, dtype=torch.bool, device=device)
+    untouched[slots[written]] = False
+    assert (flat_k[untouched] == 5.0).all() and (flat_v[untouched] == 7.0).all()
+
+
+def test_rope_cache_rejects_bad_caches():
+    q, k = torch.ones(2, 4, 8, dtype=torch.bfloat16), torch.ones(2, 2, 8, dtype=torch.bfloat16)
+    pos, slots = torch.arange(2), torch.tensor([0, 1])
+    good = torch.zeros(4, 2, 8, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="caches must be"):
+        svllm_ops.rope_cache(q, k, k.clone(), pos, slots, torch.zeros(4, 3, 8, dtype=torch.bfloat16),
+                             good, 1e4)
+    with pytest.raises(RuntimeError, match="slot_mapping"):
+        svllm_ops.rope_cache(q, k, k.clone(), pos, slots.int(), good, good.clone(), 1e4)
+    with pytest.raises(RuntimeError, match="slots past"):
+        svllm_ops.rope_cache(q, k, k.clone(), pos, torch.tensor([0, 4]), good, good.clone(), 1e4)
