@@ -55,7 +55,11 @@ PYBIND11_MODULE(svllm_ops, m) {
         py::arg("theta"), py::arg("rope_scaling") = std::nullopt);
   m.def("rope_inv_freq", &svllm::ops::rope_inv_freq, py::arg("theta"), py::arg("head_dim"),
         py::arg("rope_scaling") = std::nullopt);
-  m.def("silu_and_mul", &svllm::ops::silu_and_mul, py::arg("gate"), py::arg("up"));
+  m.def("silu_and_mul",
+        py::overload_cast<const at::Tensor&, const at::Tensor&>(&svllm::ops::silu_and_mul),
+        py::arg("gate"), py::arg("up"));
+  m.def("silu_and_mul", py::overload_cast<const at::Tensor&>(&svllm::ops::silu_and_mul),
+        py::arg("gate_up"));
   m.def("embedding", &svllm::ops::embedding, py::arg("ids"), py::arg("table"));
   m.def("read_device_error", &svllm::ops::read_device_error, py::arg("device_index"),
         py::arg("reset") = true);

@@ -3,6 +3,8 @@
 #include <ATen/Functions.h>
 #include <c10/util/Exception.h>
 
+#include <vector>
+
 #include "ops/silu_and_mul_kernels.h"
 
 namespace svllm::ops {
@@ -54,6 +56,22 @@ at::Tensor silu_and_mul(const at::Tensor& gate, const at::Tensor& up) {
       TORCH_CHECK(false, "silu_and_mul: unsupported device ", gate.device());
   }
   return out;
+}
+
+at::Tensor silu_and_mul(const at::Tensor& gate_up) {
+  TORCH_CHECK(gate_up.dim() >= 1 && gate_up.size(-1) % 2 == 0,
+              "silu_and_mul: gate_up must have an even last dimension, got shape ",
+              gate_up.sizes());
+  TORCH_CHECK(gate_up.dim() <= 2 || gate_up.is_contiguous(),
+              "silu_and_mul: gate_up must be contiguous beyond two dimensions");
+  const at::Tensor rows = gate_up.dim() == 1 ? gate_up.unsqueeze(0)
+                          : gate_up.dim() == 2 ? gate_up
+                                               : gate_up.view({-1, gate_up.size(-1)});
+  const int64_t inter = rows.size(1) / 2;
+  at::Tensor out = silu_and_mul(rows.narrow(1, 0, inter), rows.narrow(1, inter, inter));
+  std::vector<int64_t> shape(gate_up.sizes().begin(), gate_up.sizes().end());
+  shape.back() = inter;
+  return out.view(shape);
 }
 
 }  // namespace svllm::ops

@@ -15,4 +15,11 @@ namespace svllm::ops {
 // New op in the reference's op convention (docs/ROADMAP.md:40, "SiLU-and-mul").
 at::Tensor silu_and_mul(const at::Tensor& gate, const at::Tensor& up);
 
+// Definition: silu_and_mul on one concatenated gate_up projection, [..., 2 * intermediate] with
+//             gate the first half and up the second (the fused-weight layout of
+//             docs/ROADMAP.md:40, #48). No copy: the halves are passed as strided views.
+// Returns:    A new contiguous bf16 tensor [..., intermediate].
+// Throws:     As silu_and_mul, or if the last dimension is odd.
+at::Tensor silu_and_mul(const at::Tensor& gate_up);
+
 }  // namespace svllm::ops

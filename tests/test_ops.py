@@ -260,3 +260,16 @@ def test_rope_cache_rejects_bad_caches():
         svllm_ops.rope_cache(q, k, k.clone(), pos, slots.int(), good, good.clone(), 1e4)
     with pytest.raises(RuntimeError, match="slots past"):
         svllm_ops.rope_cache(q, k, k.clone(), pos, torch.tensor([0, 4]), good, good.clone(), 1e4)
+
+
+@pytest.mark.parametrize("shape", [(5, 2 * 3072), (2, 3, 2 * 512), (2 * 256,)], ids=str)
+def test_silu_and_mul_on_one_gate_up_tensor(device, shape):
+    gate_up = random_bf16(*shape, device=device, seed=24)
+    inter = shape[-1] // 2
+    out = svllm_ops.silu_and_mul(gate_up)
+    assert out.shape == (*shape[:-1], inter)
+    assert torch.equal(out, svllm_ops.silu_and_mul(gate_up[..., :inter].contiguous(),
+                                                   gate_up[..., inter:].contiguous()))
+    assert_close_bf16(out, F.silu(gate_up[..., :inter]) * gate_up[..., inter:])
+    with pytest.raises(RuntimeError, match="even last dimension"):
+        svllm_ops.silu_and_mul(gate_up[..., :-1])
