@@ -86,7 +86,9 @@ def parse_args():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=sorted(WORKLOADS), default="sweep")
+    p.add_argument("--workload", choices=sorted(WORKLOADS) + ["sampling"], default="sweep",
+                   help="sampling: greedy argmax over [tokens, 151936] bf16 logits (one op, "
+                        "not the chain)")
     p.add_argument("--tokens", type=int, default=0, help="override total tokens")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -405,8 +407,46 @@ def run_reference(args, world, rank) -> int:
     return 0
 
 
+def run_sampling(args) -> int:
+    """Greedy sampling after the LM head: argmax over bf16 logits, one op, on one GPU."""
+    import torch
+
+    import svllm_ops
+
+    vocab = QWEN3["vocab"]
+    rows = args.tokens or 1024  # 1024 x 151936 bf16 = 311 MB, above the L2
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(7)
+    logits = torch.empty(rows, vocab, device=dev, dtype=torch.bfloat16).normal_(generator=g)
+    for _ in range(args.warmup):
+        svllm_ops.argmax(logits)
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        ids = svllm_ops.argmax(logits)
+    stop.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / args.steps
+    assert torch.equal(ids, torch.argmax(logits, dim=-1))
+    nbytes = rows * vocab * 2 + rows * 8
+    peak = float(measured_peaks()["hbm_gbs"])
+    print(json.dumps({
+        "metric": "greedy sampling (argmax over logits) achieved HBM GB/s", "value":
+        round(nbytes / (ms * 1e-3) / 1e9, 1), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "argmax over LM-head logits", "rows": rows, "vocab": vocab,
+                   "l2": "no flush" if rows * vocab * 2 > 126e6 else "L2-resident"},
+        "frac_of_peak": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4),
+        "gpu_launches": args.steps}), flush=True)
+    return 0
+
+
 def main() -> int:
     args = parse_args()
+    if args.workload == "sampling":
+        return run_sampling(args)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)

@@ -226,6 +226,19 @@ int svllm_embedding_f32(float* out, const void* ids, int id_type, const float* t
                         svllm_stream stream);
 
 /*
+ * Greedy sampling: out_ids[r] = argmax over logits[r, 0:vocab] (torch.argmax semantics: the
+ * first index of the maximum, a NaN above every number). logits: [num_rows, vocab] at
+ * row_stride elements, typically the tied-embedding LM head's output after the final norm
+ * (src/model/config.h:28). out_ids: [num_rows] int64, device. A row is split over the 8 CTAs of
+ * a thread-block cluster and reduced through distributed shared memory.
+ * New op (sampling on the GPU, docs/design-spec.md:28-29).
+ */
+int svllm_argmax_bf16(const void* logits, int64_t num_rows, int64_t vocab, int64_t row_stride,
+                      int64_t* out_ids, svllm_stream stream);
+int svllm_argmax_f32(const float* logits, int64_t num_rows, int64_t vocab, int64_t row_stride,
+                     int64_t* out_ids, svllm_stream stream);
+
+/*
  * Reads (and with reset != 0 clears) the library's own error word on `device`. Synchronises
  * that device. For validation, not for the hot path.
  */

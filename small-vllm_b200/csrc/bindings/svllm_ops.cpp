@@ -12,6 +12,7 @@
 #include "ops/embedding.h"
 #include "ops/rms_norm.h"
 #include "ops/rope.h"
+#include "ops/sampling.h"
 #include "ops/silu_and_mul.h"
 
 namespace py = pybind11;
@@ -61,6 +62,9 @@ PYBIND11_MODULE(svllm_ops, m) {
   m.def("silu_and_mul", py::overload_cast<const at::Tensor&>(&svllm::ops::silu_and_mul),
         py::arg("gate_up"));
   m.def("embedding", &svllm::ops::embedding, py::arg("ids"), py::arg("table"));
+  m.def("argmax", &svllm::ops::argmax, py::arg("logits"));
+  m.def("greedy_sample", &svllm::ops::greedy_sample, py::arg("hidden"),
+        py::arg("lm_head_weight"));
   m.def("read_device_error", &svllm::ops::read_device_error, py::arg("device_index"),
         py::arg("reset") = true);
 }

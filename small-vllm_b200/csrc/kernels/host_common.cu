@@ -112,8 +112,17 @@ int blocks_per_sm(const void* func, int threads, size_t smem_bytes, int device) 
     }
   }
   if (!attr_set) {
+    // the dynamic limit is what the CTA's static shared memory leaves of the per-CTA maximum
+    cudaFuncAttributes attrs{};
+    if (cudaFuncGetAttributes(&attrs, func) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    const size_t dynamic_max = kMaxSmemPerCta > attrs.sharedSizeBytes
+                                   ? kMaxSmemPerCta - attrs.sharedSizeBytes
+                                   : 0;
     if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kMaxSmemPerCta)) != cudaSuccess) {
+                             static_cast<int>(dynamic_max)) != cudaSuccess) {
       cudaGetLastError();
       return 0;
     }

@@ -62,6 +62,8 @@ SIGNATURES = {
     "svllm_silu_and_mul_f32": [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P],
     "svllm_embedding_bf16": [_P, _P, _I, _P, _I64, _I64, _I64, _I64, _I64, _P, _P],
     "svllm_embedding_f32": [_P, _P, _I, _P, _I64, _I64, _I64, _I64, _I64, _P, _P],
+    "svllm_argmax_bf16": [_P, _I64, _I64, _I64, _P, _P],
+    "svllm_argmax_f32": [_P, _I64, _I64, _I64, _P, _P],
     "svllm_read_device_error": [_I, _I, _P],
     "svllm_set_pipeline": [ctypes.c_char_p, _I64, _I64, _I64],
 }
@@ -218,6 +220,13 @@ def embedding(out, ids, table, err=None, stream=None) -> None:
     check(fn(out.data_ptr(), ids.data_ptr(), _index_type(ids), table.data_ptr(), ids.numel(),
              vocab, hidden, os_, table.stride(0), err.data_ptr() if err is not None else None,
              _stream(stream)), "embedding")
+
+
+def argmax(out_ids, logits, stream=None) -> None:
+    rows, vocab, stride = _rows(logits)
+    fn = getattr(lib(), f"svllm_argmax_{_bf16_or_f32(logits)}")
+    check(fn(logits.data_ptr(), rows, vocab, stride, out_ids.data_ptr(), _stream(stream)),
+          "argmax")
 
 
 def read_device_error(device: int = 0, reset: bool = True) -> int:

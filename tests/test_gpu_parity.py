@@ -447,3 +447,32 @@ def test_rope_cache_slot_past_the_cache(cuda):
     assert capi.read_device_error(0, reset=True) & capi.DEVERR_BAD_INDEX
     assert torch.equal(kc[0], k[0]) and torch.equal(vc[3], v[2])
     assert not kc[[1, 2, 4, 5, 6, 7]].any()
+
+
+# ---------------------------------------------------------------------------------------------
+# greedy sampling (argmax), through the C ABI, against numpy's argmax (first maximum; NaN wins)
+
+@pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
+@pytest.mark.parametrize("rows, vocab", [(1, 151936), (256, 151936), (1024, 128256), (3, 1001),
+                                         (64, 8)], ids=str)
+def test_argmax(cuda, dt, rows, vocab):
+    logits = random_t(rows, vocab, dtype=dt, device=cuda, seed=60, scale=3.0)
+    ids = torch.empty(rows, dtype=torch.int64, device=cuda)
+    capi.argmax(ids, logits)
+    want = np.argmax(logits.float().cpu().numpy(), axis=-1)
+    assert np.array_equal(ids.cpu().numpy(), want)
+    assert torch.equal(ids, torch.argmax(logits, dim=-1))
+
+
+def test_argmax_strided_rows_and_edge_values(cuda):
+    big = random_t(40, 5000 + 8, device=cuda, seed=61)
+    logits = big[:, :5000]  # row stride 5008
+    logits[0, 4999] = 100.0
+    logits[1, :] = 0.0
+    logits[1, [7, 4000]] = 5.0
+    logits[2, 333] = float("nan")
+    logits[3, :] = float("-inf")
+    ids = torch.empty(40, dtype=torch.int64, device=cuda)
+    capi.argmax(ids, logits)
+    assert ids[:4].tolist() == [4999, 7, 333, 0]
+    assert torch.equal(ids[4:], torch.argmax(logits[4:], dim=-1))

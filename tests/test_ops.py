@@ -273,3 +273,38 @@ def test_silu_and_mul_on_one_gate_up_tensor(device, shape):
     assert_close_bf16(out, F.silu(gate_up[..., :inter]) * gate_up[..., inter:])
     with pytest.raises(RuntimeError, match="even last dimension"):
         svllm_ops.silu_and_mul(gate_up[..., :-1])
+
+
+# ---------------------------------------------------------------------------------------------
+# greedy sampling
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32], ids=["bf16", "f32"])
+@pytest.mark.parametrize("shape", [(1, 151936), (7, 1000), (3, 4, 700), (2, 17)], ids=str)
+def test_argmax(device, dtype, shape):
+    logits = random_t(*shape, dtype=dtype, device=device, seed=25)
+    assert torch.equal(svllm_ops.argmax(logits), torch.argmax(logits, dim=-1))
+
+
+def test_argmax_ties_nan_and_infinities(device):
+    logits = torch.zeros(4, 5000, dtype=torch.bfloat16, device=device)
+    logits[0, [17, 300, 4999]] = 3.0           # a tie: the first index wins
+    logits[1, 123] = float("nan")              # NaN beats any number
+    logits[1, 4000] = float("nan")
+    logits[1, 10] = float("inf")
+    logits[2, :] = float("-inf")               # all -inf: index 0
+    logits[3, 4999] = 1.0                      # the last element
+    assert svllm_ops.argmax(logits).tolist() == [17, 123, 0, 4999]
+
+
+def test_greedy_sample_with_a_tied_lm_head(device):
+    hidden = random_bf16(6, 256, device=device, seed=26)
+    table = random_t(3000, 256, device=device, seed=27, scale=0.02)
+    logits = hidden @ table.t()
+    assert torch.equal(svllm_ops.greedy_sample(hidden, table), torch.argmax(logits, dim=-1))
+
+
+def test_argmax_rejects_bad_inputs():
+    with pytest.raises(RuntimeError, match="bf16 or fp32"):
+        svllm_ops.argmax(torch.zeros(2, 3, dtype=torch.int32))
+    with pytest.raises(RuntimeError, match="contiguous last"):
+        svllm_ops.argmax(torch.zeros(8, 2).t())
