@@ -125,7 +125,23 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kArgmaxTh
     const S* x = static_cast<const S*>(a.logits) + row * a.stride;
     Best best{__int_as_float(0xff800000), INT64_MAX};  // -inf, an index no element has
     if (a.vec) {
-      for (int64_t u = u_begin + threadIdx.x; u < u_end; u += blockDim.x) {
+      // four 16-byte loads in flight per thread; `beats` is a total order, so the order in
+      // which candidates are taken does not change the result
+      const int64_t step = blockDim.x;
+      int64_t u = u_begin + threadIdx.x;
+      for (; u + 3 * step < u_end; u += 4 * step) {
+        uint4 raw[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) raw[q] = ld_global_nc_v4(x + (u + q * step) * kVec);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float f[kVec];
+          unpack<E>(raw[q], f);
+#pragma unroll
+          for (int e = 0; e < kVec; ++e) take(best, f[e], (u + q * step) * kVec + e);
+        }
+      }
+      for (; u < u_end; u += step) {
         float f[kVec];
         unpack<E>(ld_global_nc_v4(x + u * kVec), f);
 #pragma unroll
