@@ -3,12 +3,11 @@
 //
 // This is the step after the final norm and the tied-embedding LM head (the reference's
 // src/model/config.h:28 tie_word_embeddings; sampling "on GPU", docs/design-spec.md:28-29):
-// logits [rows, vocab] with vocab ~150k are read once. A row is split over the 8 CTAs of a
-// thread-block cluster (on 8 SMs), so even a single-sequence decode step streams its 300 KB row
-// from eight SMs at once. Each CTA reduces its slice with 16-byte loads, shuffles and one shared
-// memory pass; the cluster's eight partial results are then combined by CTA 0 reading the
-// others' shared memory through the cluster's distributed shared memory. No global scratch,
-// no atomics, no second launch.
+// logits [rows, vocab] with vocab ~150k are read once, 16-byte loads, eight in flight per
+// thread. A row goes to one CTA, or, when there are too few rows to keep enough loads in flight
+// (a decode step's batch), to the 2, 4 or 8 CTAs of a thread-block cluster, whose partial
+// results are combined through distributed shared memory: even one sequence streams its 300 KB
+// row from eight SMs. No global scratch, no atomics, no second launch.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -19,8 +18,10 @@
 namespace svllm::k {
 namespace {
 
-constexpr int kClusterCtas = 8;  // the portable cluster size
-constexpr int kArgmaxThreads = 512;
+constexpr int kMaxCtasPerRow = 8;  // the portable cluster size
+constexpr int kMinThreads = 256;
+constexpr int kMaxThreads = 1024;
+constexpr int kLoadsInFlight = 8;
 
 struct ArgmaxArgs {
   const void* logits;
@@ -36,17 +37,14 @@ struct Best {
   int64_t i;
 };
 
-// a beats b: larger value, NaN above every number, the lower index on ties.
+constexpr float kNegInf = -__builtin_huge_valf();
+
+// a beats b: NaN above every number, then the larger value, then the lower index.
 __device__ __forceinline__ bool beats(const Best& a, const Best& b) {
   const bool an = a.v != a.v, bn = b.v != b.v;
   if (an != bn) return an;
   if (an || a.v == b.v) return a.i < b.i;
   return a.v > b.v;
-}
-
-__device__ __forceinline__ void take(Best& best, float v, int64_t i) {
-  const Best c{v, i};
-  if (beats(c, best)) best = c;
 }
 
 __device__ __forceinline__ Best warp_best(Best b) {
@@ -60,21 +58,187 @@ __device__ __forceinline__ Best warp_best(Best b) {
   return b;
 }
 
+// The larger of a and b, NaN if either is NaN.
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
+// c replaces the running maximum m of earlier candidates: it is larger, or it is the first NaN.
+__device__ __forceinline__ bool exceeds(float c, float m) { return c > m || (c != c && m == m); }
+
+// f is the value v (-0 == +0; every NaN matches a NaN).
+__device__ __forceinline__ bool same(float f, float v) { return f == v || (f != f && v != v); }
+
+// The largest element of whole 16-byte vectors, reduced word-wise in the storage type (one
+// instruction for two bf16 elements) and finished in fp32; NaN if any element is NaN.
+template <class E>
+struct VecMax;
+
+template <>
+struct VecMax<Bf16> {
+  static constexpr uint32_t kNegInfWord = 0xff80ff80u;  // -inf in both halves
+  __device__ static __forceinline__ uint32_t combine(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+  }
+  __device__ static __forceinline__ float finish(uint32_t w) {
+    return max_nan(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  }
+};
+
+template <>
+struct VecMax<F32> {
+  static constexpr uint32_t kNegInfWord = 0xff800000u;
+  __device__ static __forceinline__ uint32_t combine(uint32_t a, uint32_t b) {
+    return __float_as_uint(max_nan(__uint_as_float(a), __uint_as_float(b)));
+  }
+  __device__ static __forceinline__ float finish(uint32_t w) { return __uint_as_float(w); }
+};
+
+template <class E, int N>
+__device__ __forceinline__ float vectors_max(const uint4 (&raw)[N]) {
+  uint32_t w[4 * N];
+#pragma unroll
+  for (int q = 0; q < N; ++q) {
+    w[4 * q] = raw[q].x;
+    w[4 * q + 1] = raw[q].y;
+    w[4 * q + 2] = raw[q].z;
+    w[4 * q + 3] = raw[q].w;
+  }
+  // pairwise tree: 4N words to one
+#pragma unroll
+  for (int width = 2 * N; width >= 1; width /= 2) {
+#pragma unroll
+    for (int j = 0; j < width; ++j) w[j] = VecMax<E>::combine(w[j], w[j + width]);
+  }
+  return VecMax<E>::finish(w[0]);
+}
+
+// One thread's pass over its units [u_begin, u_end) of a row (units u_begin + threadIdx.x + k *
+// blockDim.x), in chunks of kLoadsInFlight units: the largest value `v` and the chunk holding
+// its first occurrence, `n` units starting at unit `u` (u = -1: the thread has no units).
+// Candidates arrive in increasing index order, so a strict comparison keeps the first maximum;
+// a chunk's maximum costs about one instruction per element pair, and the exact index is looked
+// up afterwards, only by the threads that hold the row's maximum.
+struct Scan {
+  float v;
+  int64_t u;
+  int n;
+};
+
+// The last chunk a thread loaded, kept in registers: when it holds the maximum (always, for a
+// thread with one chunk) the index lookup needs no second load.
+struct Chunk {
+  uint4 raw[kLoadsInFlight];
+  int64_t u = -1;
+};
+
+template <class E>
+__device__ __forceinline__ Scan scan_slice(const typename E::Storage* x, int64_t u_begin,
+                                           int64_t u_end, int vec, Chunk& last) {
+  constexpr int kVec = E::kPerVec;
+  const int64_t step = blockDim.x;
+  int64_t u = u_begin + threadIdx.x;
+  // -inf in the thread's first unit: if nothing exceeds it, every element is -inf and the
+  // first one is the answer
+  Scan s{kNegInf, u < u_end ? u : -1, 1};
+  if (vec) {
+    constexpr uint32_t kFill = VecMax<E>::kNegInfWord;  // units past the slice end read -inf
+    for (; u < u_end; u += kLoadsInFlight * step) {
+#pragma unroll
+      for (int q = 0; q < kLoadsInFlight; ++q) {
+        const int64_t uq = u + q * step;
+        last.raw[q] = uq < u_end ? ld_global_nc_v4(x + uq * kVec)
+                                 : make_uint4(kFill, kFill, kFill, kFill);
+      }
+      last.u = u;
+      const float c = vectors_max<E>(last.raw);
+      if (exceeds(c, s.v)) {
+        const int64_t n = (u_end - u + step - 1) / step;
+        s = Scan{c, u, static_cast<int>(n < kLoadsInFlight ? n : kLoadsInFlight)};
+      }
+    }
+  } else {
+    for (; u < u_end; u += step) {
+      const float c = E::to_float(x[u]);
+      if (exceeds(c, s.v)) s = Scan{c, u, 1};
+    }
+  }
+  return s;
+}
+
+// The first index in the thread's chunk `s` whose element is v (the chunk holds one), from the
+// registers when `last` is that chunk, else from memory.
+template <class E>
+__device__ int64_t first_index_of(const typename E::Storage* x, const Scan& s, float v, int vec,
+                                  const Chunk& last) {
+  constexpr int kVec = E::kPerVec;
+  const int64_t step = blockDim.x;
+  if (vec && last.u == s.u) {
+    int64_t found = INT64_MAX;
+    // backwards, so that the last assignment is the first match
+#pragma unroll
+    for (int q = kLoadsInFlight - 1; q >= 0; --q) {
+      float f[kVec];
+      unpack<E>(last.raw[q], f);
+#pragma unroll
+      for (int e = kVec - 1; e >= 0; --e) {
+        if (q < s.n && same(f[e], v)) found = (s.u + q * step) * kVec + e;
+      }
+    }
+    return found;
+  }
+  for (int q = 0; q < s.n; ++q) {
+    const int64_t unit = s.u + q * step;
+    if (vec) {
+      float f[kVec];
+      unpack<E>(ld_global_nc_v4(x + unit * kVec), f);
+#pragma unroll
+      for (int e = 0; e < kVec; ++e) {
+        if (same(f[e], v)) return unit * kVec + e;
+      }
+    } else if (same(E::to_float(x[unit]), v)) {
+      return unit;
+    }
+  }
+  return INT64_MAX;
+}
+
+// The CTA's (largest value, first index of it) over this row's slice; every thread returns it.
+// Two barriers: one after the value reduction, one after the index reduction; each reduction
+// has its own scratch, so the next row's writes cannot overtake this row's reads.
+template <class E>
+__device__ __forceinline__ Best cta_best(const typename E::Storage* x, const Scan& s, int vec,
+                                         const Chunk& last, float* red_v, int64_t* red_i) {
+  const int warp = threadIdx.x / kWarpSize;
+  const int lane = threadIdx.x % kWarpSize;
+  const int warps = blockDim.x / kWarpSize;
+  float v = s.v;
+#pragma unroll
+  for (int off = 16; off > 0; off /= 2) v = max_nan(v, __shfl_xor_sync(0xffffffffu, v, off));
+  if (lane == 0) red_v[warp] = v;
+  __syncthreads();
+  v = lane < warps ? red_v[lane] : kNegInf;
+#pragma unroll
+  for (int off = 16; off > 0; off /= 2) v = max_nan(v, __shfl_xor_sync(0xffffffffu, v, off));
+
+  int64_t i = (s.u >= 0 && same(s.v, v)) ? first_index_of<E>(x, s, v, vec, last) : INT64_MAX;
+#pragma unroll
+  for (int off = 16; off > 0; off /= 2) i = min(i, __shfl_xor_sync(0xffffffffu, i, off));
+  if (lane == 0) red_i[warp] = i;
+  __syncthreads();
+  i = lane < warps ? red_i[lane] : INT64_MAX;
+#pragma unroll
+  for (int off = 16; off > 0; off /= 2) i = min(i, __shfl_xor_sync(0xffffffffu, i, off));
+  return Best{v, i};
+}
+
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t num_clusters_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
   return r;
 }
 
@@ -102,82 +266,103 @@ __device__ __forceinline__ int64_t ld_cluster_s64(uint32_t addr) {
   return v;
 }
 
-template <class E>
-__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kArgmaxThreads)
-    argmax_kernel(const ArgmaxArgs a) {
+// Row r goes to CTAs [r * kCtas, (r + 1) * kCtas), one cluster when kCtas > 1; every CTA of a
+// cluster runs the same rows, so all meet every cluster barrier.
+template <class E, int kCtas>
+__global__ void __launch_bounds__(kMaxThreads) argmax_kernel(const ArgmaxArgs a) {
   using S = typename E::Storage;
-  constexpr int kVec = E::kPerVec;
-  __shared__ float warp_v[kArgmaxThreads / kWarpSize];
-  __shared__ int64_t warp_i[kArgmaxThreads / kWarpSize];
+  __shared__ float red_v[kMaxThreads / kWarpSize];
+  __shared__ int64_t red_i[kMaxThreads / kWarpSize];
   __shared__ float cta_v;
   __shared__ int64_t cta_i;
 
-  const uint32_t rank = cluster_ctarank();
-  const int warp = threadIdx.x / kWarpSize;
-  const int lane = threadIdx.x % kWarpSize;
-  // this CTA's slice of every row, in whole vectors
-  const int64_t units = a.vec ? a.vocab / kVec : a.vocab;
-  const int64_t per = (units + kClusterCtas - 1) / kClusterCtas;
+  const uint32_t rank = kCtas > 1 ? cluster_ctarank() : 0;
+  // this CTA's slice of every row, in whole units
+  const int64_t units = a.vec ? a.vocab / E::kPerVec : a.vocab;
+  const int64_t per = (units + kCtas - 1) / kCtas;
   const int64_t u_begin = min(units, per * rank);
   const int64_t u_end = min(units, u_begin + per);
+  const int64_t groups = gridDim.x / kCtas;
 
-  for (int64_t row = cluster_id_x(); row < a.rows; row += num_clusters_x()) {
+  for (int64_t row = blockIdx.x / kCtas; row < a.rows; row += groups) {
     const S* x = static_cast<const S*>(a.logits) + row * a.stride;
-    Best best{__int_as_float(0xff800000), INT64_MAX};  // -inf, an index no element has
-    if (a.vec) {
-      // four 16-byte loads in flight per thread; `beats` is a total order, so the order in
-      // which candidates are taken does not change the result
-      const int64_t step = blockDim.x;
-      int64_t u = u_begin + threadIdx.x;
-      for (; u + 3 * step < u_end; u += 4 * step) {
-        uint4 raw[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) raw[q] = ld_global_nc_v4(x + (u + q * step) * kVec);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float f[kVec];
-          unpack<E>(raw[q], f);
-#pragma unroll
-          for (int e = 0; e < kVec; ++e) take(best, f[e], (u + q * step) * kVec + e);
-        }
-      }
-      for (; u < u_end; u += step) {
-        float f[kVec];
-        unpack<E>(ld_global_nc_v4(x + u * kVec), f);
-#pragma unroll
-        for (int e = 0; e < kVec; ++e) take(best, f[e], u * kVec + e);
-      }
+    Chunk last;
+    const Scan sc = scan_slice<E>(x, u_begin, u_end, a.vec, last);
+    const Best b = cta_best<E>(x, sc, a.vec, last, red_v, red_i);
+    if constexpr (kCtas == 1) {
+      if (threadIdx.x == 0) a.out[row] = b.i;
     } else {
-      for (int64_t u = u_begin + threadIdx.x; u < u_end; u += blockDim.x) {
-        take(best, E::to_float(x[u]), u);
-      }
-    }
-    best = warp_best(best);
-    if (lane == 0) {
-      warp_v[warp] = best.v;
-      warp_i[warp] = best.i;
-    }
-    __syncthreads();
-    if (warp == 0) {
-      Best b{__int_as_float(0xff800000), INT64_MAX};
-      if (lane < static_cast<int>(blockDim.x / kWarpSize)) b = Best{warp_v[lane], warp_i[lane]};
-      b = warp_best(b);
-      if (lane == 0) {
+      if (threadIdx.x == 0) {
         cta_v = b.v;
         cta_i = b.i;
       }
-    }
-    cluster_sync();  // every CTA's partial result is visible cluster-wide
-    if (rank == 0 && threadIdx.x == 0) {
-      Best b{cta_v, cta_i};
-      for (uint32_t r = 1; r < kClusterCtas; ++r) {
-        const Best o{ld_cluster_f32(map_shared(&cta_v, r)), ld_cluster_s64(map_shared(&cta_i, r))};
-        if (beats(o, b)) b = o;
+      cluster_sync();  // every CTA's partial result is visible cluster-wide
+      if (rank == 0 && threadIdx.x < kWarpSize) {
+        // lane r reads CTA r's result (all loads in flight at once), then one warp merge
+        Best o{kNegInf, INT64_MAX};
+        if (threadIdx.x < kCtas) {
+          o = Best{ld_cluster_f32(map_shared(&cta_v, threadIdx.x)),
+                   ld_cluster_s64(map_shared(&cta_i, threadIdx.x))};
+        }
+        o = warp_best(o);
+        if (threadIdx.x == 0) a.out[row] = o.i;
       }
-      a.out[row] = b.i;
+      cluster_sync();  // CTA 0 has read every result before a CTA moves on or exits
     }
-    cluster_sync();  // CTA 0 has read everyone's result before the next row overwrites it
   }
+}
+
+// A launch shape for kCtas CTAs per row: threads per CTA and the chunk rounds the longest
+// thread runs (its chunks times the waves of CTAs). Threads: enough that a thread's share of its
+// row slice is one chunk, between kMinThreads and kMaxThreads in steps of two warps, and no more
+// than lets every CTA start in the first wave.
+struct Shape {
+  int threads;
+  int64_t rounds;
+};
+
+template <class E, int kCtas>
+Shape shape_for(const ArgmaxArgs& a, int device) {
+  const void* func = reinterpret_cast<const void*>(argmax_kernel<E, kCtas>);
+  const int64_t sms = sm_count(device);
+  const int64_t units = a.vec ? a.vocab / E::kPerVec : a.vocab;
+  const int64_t slice = (units + kCtas - 1) / kCtas;
+  const int64_t ctas = a.rows * kCtas;
+  const int64_t need_per_sm = (ctas + sms - 1) / sms;
+  constexpr int kStep = 2 * kWarpSize;
+  int64_t t = round_up((slice + kLoadsInFlight - 1) / kLoadsInFlight, kStep);
+  t = t < kMinThreads ? kMinThreads : (t > kMaxThreads ? kMaxThreads : t);
+  int per_sm = blocks_per_sm(func, static_cast<int>(t), 0, device);
+  while (t > kMinThreads && per_sm < need_per_sm) {
+    t -= kStep;
+    per_sm = blocks_per_sm(func, static_cast<int>(t), 0, device);
+  }
+  const int64_t resident = sms * (per_sm > 0 ? per_sm : 1);
+  const int64_t waves = (ctas + resident - 1) / resident;
+  const int64_t chunks = (slice + t * kLoadsInFlight - 1) / (t * kLoadsInFlight);
+  return Shape{static_cast<int>(t), chunks * waves};
+}
+
+template <class E, int kCtas>
+int launch_split(const ArgmaxArgs& a, int threads, cudaStream_t stream) {
+  // kCtas CTAs per row, up to 2^30 CTAs; rows beyond that are taken in a grid-stride loop
+  constexpr int64_t kMaxGroups = (int64_t{1} << 30) / kCtas;
+  const int64_t groups = a.rows < kMaxGroups ? a.rows : kMaxGroups;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(groups * kCtas));
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kCtas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = kCtas > 1 ? 1 : 0;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, argmax_kernel<E, kCtas>, a);
+  const int status = launch_status();  // also clears the error a failed launch leaves
+  return err == cudaSuccess ? status : SVLLM_ERR_LAUNCH;
 }
 
 template <class E>
@@ -200,14 +385,28 @@ int launch_argmax(const void* logits, int64_t rows, int64_t vocab, int64_t strid
   a.stride = stride;
   a.vec = aligned16(logits) && (stride * sizeof(S)) % 16 == 0 && (vocab * sizeof(S)) % 16 == 0;
 
-  // one cluster per row, as many clusters as fit on the GPU at once
-  const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(argmax_kernel<E>),
-                                   kArgmaxThreads, 0, device);
-  const int64_t max_clusters =
-      static_cast<int64_t>(sm_count(device)) * (per_sm > 0 ? per_sm : 1) / kClusterCtas;
-  const int64_t clusters = rows < max_clusters ? rows : (max_clusters > 0 ? max_clusters : 1);
-  argmax_kernel<E><<<static_cast<unsigned>(clusters * kClusterCtas), kArgmaxThreads, 0, stream>>>(a);
-  return launch_status();
+  // Many rows: a CTA per row, several per SM, each thread streaming several chunks. Fewer
+  // rows: the split (1, 2, 4 or 8 CTAs per row) and CTA size with the fewest chunk rounds; on a
+  // tie, the one with the most threads (the most SMs at work), then the smaller split (fewer
+  // cluster barriers).
+  if (rows >= 2 * static_cast<int64_t>(sm_count(device))) {
+    return launch_split<E, 1>(a, kMinThreads, stream);
+  }
+  const Shape shapes[4] = {shape_for<E, 1>(a, device), shape_for<E, 2>(a, device),
+                           shape_for<E, 4>(a, device), shape_for<E, kMaxCtasPerRow>(a, device)};
+  int pick = 0;
+  for (int k = 1; k < 4; ++k) {
+    const Shape& c = shapes[k];
+    const Shape& p = shapes[pick];
+    const int64_t c_threads = (rows << k) * c.threads, p_threads = (rows << pick) * p.threads;
+    if (c.rounds < p.rounds || (c.rounds == p.rounds && c_threads > p_threads)) pick = k;
+  }
+  switch (pick) {
+    case 0: return launch_split<E, 1>(a, shapes[0].threads, stream);
+    case 1: return launch_split<E, 2>(a, shapes[1].threads, stream);
+    case 2: return launch_split<E, 4>(a, shapes[2].threads, stream);
+    default: return launch_split<E, kMaxCtasPerRow>(a, shapes[3].threads, stream);
+  }
 }
 
 }  // namespace

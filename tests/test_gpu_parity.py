@@ -454,7 +454,8 @@ def test_rope_cache_slot_past_the_cache(cuda):
 
 @pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
 @pytest.mark.parametrize("rows, vocab", [(1, 151936), (256, 151936), (1024, 128256), (3, 1001),
-                                         (64, 8)], ids=str)
+                                         (64, 8), (5, 1024), (37, 151936), (73, 151936),
+                                         (2000, 32000)], ids=str)
 def test_argmax(cuda, dt, rows, vocab):
     logits = random_t(rows, vocab, dtype=dt, device=cuda, seed=60, scale=3.0)
     ids = torch.empty(rows, dtype=torch.int64, device=cuda)
@@ -476,3 +477,29 @@ def test_argmax_strided_rows_and_edge_values(cuda):
     capi.argmax(ids, logits)
     assert ids[:4].tolist() == [4999, 7, 333, 0]
     assert torch.equal(ids[4:], torch.argmax(logits[4:], dim=-1))
+
+
+@pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
+@pytest.mark.parametrize("rows, vocab", [(4, 151936), (100, 151936), (200, 151937),
+                                         (400, 151936)], ids=str)
+def test_argmax_edge_rows_every_split(cuda, dt, rows, vocab):
+    """Row counts that give one row to 8, 4, 2 and 1 CTAs (148 SMs); the odd vocabulary takes
+    the element-wise path. Planted rows: every element tied, a row of -inf, ties across the
+    slice boundaries of the CTAs sharing a row, a maximum in the last element, and NaNs after
+    the maximum (the first NaN wins)."""
+    logits = random_t(rows, vocab, dtype=dt, device=cuda, seed=62, scale=2.0)
+    logits[0, :] = 1.0
+    logits[1, :] = float("-inf")
+    logits[2, vocab // 8 - 1] = 50.0
+    logits[2, vocab // 2] = 50.0
+    logits[2, vocab - 1] = 50.0
+    logits[3, vocab - 1] = 60.0
+    if rows > 4:
+        logits[4, 10] = 70.0
+        logits[4, vocab // 3] = float("nan")
+        logits[4, vocab - 2] = float("nan")
+    ids = torch.empty(rows, dtype=torch.int64, device=cuda)
+    capi.argmax(ids, logits)
+    want = [0, 0, vocab // 8 - 1, vocab - 1] + ([vocab // 3] if rows > 4 else [])
+    assert ids[:len(want)].tolist() == want
+    assert torch.equal(ids, torch.argmax(logits, dim=-1))
