@@ -86,9 +86,15 @@ def parse_args():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=sorted(WORKLOADS) + ["sampling"], default="sweep",
+    p.add_argument("--workload", choices=sorted(WORKLOADS) + ["sampling", "model-decode"],
+                   default="sweep",
                    help="sampling: greedy argmax over [tokens, 151936] bf16 logits (one op, "
-                        "not the chain)")
+                        "not the chain); model-decode: Qwen3-0.6B decode steps through the "
+                        "model forward, eager and from CUDA graphs")
+    p.add_argument("--batches", default="1,8,64,256",
+                   help="model-decode: comma-separated decode batch sizes")
+    p.add_argument("--context", type=int, default=512,
+                   help="model-decode: KV-cache tokens per request")
     p.add_argument("--tokens", type=int, default=0, help="override total tokens")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -459,10 +465,105 @@ def run_sampling(args) -> int:
     return 0
 
 
+def model_weights(cfg: dict, layers: int, device, seed: int = 1234) -> dict:
+    """Random Hugging Face-named weights of a Qwen3 model: projections N(0, 0.02), norm weights
+    1 + N(0, 0.1), tied embedding."""
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    h, hq, hk, d, i, v = (cfg["hidden"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"],
+                          cfg["inter"], cfg["vocab"])
+
+    def proj(*shape):
+        return (torch.randn(*shape, device=device, generator=g) * 0.02).to(torch.bfloat16)
+
+    def norm(n):
+        return (1 + 0.1 * torch.randn(n, device=device, generator=g)).to(torch.bfloat16)
+
+    w = {"model.embed_tokens.weight": proj(v, h), "model.norm.weight": norm(h)}
+    for layer in range(layers):
+        p = f"model.layers.{layer}."
+        w.update({p + "input_layernorm.weight": norm(h),
+                  p + "post_attention_layernorm.weight": norm(h),
+                  p + "self_attn.q_proj.weight": proj(hq * d, h),
+                  p + "self_attn.k_proj.weight": proj(hk * d, h),
+                  p + "self_attn.v_proj.weight": proj(hk * d, h),
+                  p + "self_attn.o_proj.weight": proj(h, hq * d),
+                  p + "self_attn.q_norm.weight": norm(d),
+                  p + "self_attn.k_norm.weight": norm(d),
+                  p + "mlp.gate_proj.weight": proj(i, h),
+                  p + "mlp.up_proj.weight": proj(i, h),
+                  p + "mlp.down_proj.weight": proj(h, i)})
+    return w
+
+
+def run_model_decode(args) -> int:
+    """Decode steps of Qwen3-0.6B (28 layers, random weights) through svllm_ops.Model: the fused
+    ops around torch GEMMs and a LibTorch attention over a paged KV cache of `--context` random
+    tokens per request, greedy sampling included; eager and replayed from CUDA graphs."""
+    import torch
+
+    import svllm_ops
+
+    cfg, layers, block = QWEN3, 28, 16
+    dev = torch.device("cuda", 0)
+    batches = [int(b) for b in args.batches.split(",")]
+    blocks_per_seq = -(-args.context // block)
+    model = svllm_ops.Model(svllm_ops.ModelConfig(
+        vocab_size=cfg["vocab"], hidden_size=cfg["hidden"], intermediate_size=cfg["inter"],
+        num_layers=layers, num_heads=cfg["heads"], num_kv_heads=cfg["kv_heads"],
+        head_dim=cfg["head_dim"], rms_norm_eps=cfg["eps"], rope_theta=cfg["theta"],
+        tie_word_embeddings=True, qk_norm=True), model_weights(cfg, layers, dev))
+    model.allocate_kv_cache(max(batches) * blocks_per_seq, block)
+    g = torch.Generator(device=dev).manual_seed(3)
+    for k, v in zip(model.k_cache, model.v_cache):
+        k.normal_(generator=g)
+        v.normal_(generator=g)
+    graphs = svllm_ops.DecodeGraphs(model, max_num_seqs=max(batches),
+                                    max_blocks_per_seq=blocks_per_seq, batch_sizes=batches)
+    for b in batches:
+        tables = torch.arange(b * blocks_per_seq, device=dev, dtype=torch.int32).view(b, -1)
+        seq_lens = torch.full((b,), args.context, device=dev, dtype=torch.int32)
+        pos = seq_lens.long() - 1
+        slots = tables[:, -1].long() * block + pos % block
+        ids = torch.randint(0, cfg["vocab"], (b,), device=dev, generator=g)
+        step = dict(ids=ids, positions=pos, slot_mapping=slots, block_tables=tables,
+                    seq_lens=seq_lens)
+        times = {}
+        for mode, fn in (("eager", model.decode), ("graph", graphs.step)):
+            for _ in range(args.warmup):
+                out = fn(**step)
+            torch.cuda.synchronize()
+            start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            for _ in range(args.steps):
+                out = fn(**step)
+            stop.record()
+            torch.cuda.synchronize()
+            times[mode] = start.elapsed_time(stop) / args.steps
+            if mode == "eager":
+                eager_out = out
+        assert torch.equal(out, eager_out)
+        print(json.dumps({
+            "metric": "Qwen3-0.6B decode throughput (tokens/s)",
+            "value": round(b / (times["graph"] * 1e-3), 1), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(times["graph"], 4), "eager_ms_per_step": round(times["eager"], 4),
+            "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic (random weights, random KV cache)",
+            "config": {"workload": "decode step through the model forward (28 layers, greedy)",
+                       "batch": b, "context": args.context, "block_size": block,
+                       "timing": "CUDA graph replay; eager alongside"}}), flush=True)
+    del graphs
+    return 0
+
+
 def main() -> int:
     args = parse_args()
     if args.workload == "sampling":
         return run_sampling(args)
+    if args.workload == "model-decode":
+        return run_model_decode(args)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)

@@ -2,8 +2,9 @@
 
 Products (all inside this directory, so they travel with the source tree):
   lib/libsvllm_kernels.so   the sm_100a CUDA kernels behind the C ABI in include/svllm_kernels.h
-  python/svllm_ops*.so      the LibTorch op layer + pybind11 module `svllm_ops` (the reference's
-                            binding name, bindings/svllm_ops.cpp:11), linked to the library above
+  python/svllm_ops*.so      the LibTorch op layer, the model forward that calls it, and the
+                            pybind11 module `svllm_ops` (the reference's binding name,
+                            bindings/svllm_ops.cpp:11), linked to the library above
 
 Usage: python small-vllm_b200/build.py [--force] [--jobs N]
 Only sources newer than their outputs are rebuilt. nvcc cross-compiles for sm_100a without a
@@ -122,6 +123,7 @@ def _torch_flags() -> tuple[list[str], list[str]]:
         "-ltorch_cpu",
         "-ltorch_python",
         "-lc10_cuda",
+        "-ltorch_cuda",
         f"-L{LIB_DIR}",
         "-lsvllm_kernels",
         "-Wl,-rpath,$ORIGIN/../lib",
@@ -134,7 +136,8 @@ def build_ops(force: bool, jobs: int) -> Path:
     """Compiles the LibTorch op layer and the pybind11 module svllm_ops."""
     # The system g++ ships OpenMP's spec files; a toolchain on CXX may not.
     cxx = "/usr/bin/g++" if Path("/usr/bin/g++").exists() else os.environ.get("CXX", "g++")
-    sources = sorted((CSRC / "ops").rglob("*.cpp")) + sorted((CSRC / "bindings").glob("*.cpp"))
+    sources = (sorted((CSRC / "ops").rglob("*.cpp")) + sorted((CSRC / "model").glob("*.cpp")) +
+               sorted((CSRC / "bindings").glob("*.cpp")))
     headers = (sorted((CSRC / "ops").rglob("*.h")) + sorted((CSRC / "model").glob("*.h")) +
                [INCLUDE / "svllm_kernels.h"])
     obj_dir = BUILD / "ops"

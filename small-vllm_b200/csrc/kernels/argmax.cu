@@ -5,7 +5,7 @@
 // src/model/config.h:28 tie_word_embeddings; sampling "on GPU", docs/design-spec.md:28-29):
 // logits [rows, vocab] with vocab ~150k are read once, 16-byte loads, eight in flight per
 // thread. A row goes to one CTA, or, when there are too few rows to keep enough loads in flight
-// (a decode step's batch), to the 2, 4 or 8 CTAs of a thread-block cluster, whose partial
+// (a decode step's batch), to the 4 or 8 CTAs of a thread-block cluster, whose partial
 // results are combined through distributed shared memory: even one sequence streams its 300 KB
 // row from eight SMs. No global scratch, no atomics, no second launch.
 #include <cuda_runtime.h>
@@ -19,7 +19,6 @@ namespace svllm::k {
 namespace {
 
 constexpr int kMaxCtasPerRow = 8;  // the portable cluster size
-constexpr int kMinThreads = 256;
 constexpr int kMaxThreads = 1024;
 constexpr int kLoadsInFlight = 8;
 
@@ -312,37 +311,6 @@ __global__ void __launch_bounds__(kMaxThreads) argmax_kernel(const ArgmaxArgs a)
   }
 }
 
-// A launch shape for kCtas CTAs per row: threads per CTA and the chunk rounds the longest
-// thread runs (its chunks times the waves of CTAs). Threads: enough that a thread's share of its
-// row slice is one chunk, between kMinThreads and kMaxThreads in steps of two warps, and no more
-// than lets every CTA start in the first wave.
-struct Shape {
-  int threads;
-  int64_t rounds;
-};
-
-template <class E, int kCtas>
-Shape shape_for(const ArgmaxArgs& a, int device) {
-  const void* func = reinterpret_cast<const void*>(argmax_kernel<E, kCtas>);
-  const int64_t sms = sm_count(device);
-  const int64_t units = a.vec ? a.vocab / E::kPerVec : a.vocab;
-  const int64_t slice = (units + kCtas - 1) / kCtas;
-  const int64_t ctas = a.rows * kCtas;
-  const int64_t need_per_sm = (ctas + sms - 1) / sms;
-  constexpr int kStep = 2 * kWarpSize;
-  int64_t t = round_up((slice + kLoadsInFlight - 1) / kLoadsInFlight, kStep);
-  t = t < kMinThreads ? kMinThreads : (t > kMaxThreads ? kMaxThreads : t);
-  int per_sm = blocks_per_sm(func, static_cast<int>(t), 0, device);
-  while (t > kMinThreads && per_sm < need_per_sm) {
-    t -= kStep;
-    per_sm = blocks_per_sm(func, static_cast<int>(t), 0, device);
-  }
-  const int64_t resident = sms * (per_sm > 0 ? per_sm : 1);
-  const int64_t waves = (ctas + resident - 1) / resident;
-  const int64_t chunks = (slice + t * kLoadsInFlight - 1) / (t * kLoadsInFlight);
-  return Shape{static_cast<int>(t), chunks * waves};
-}
-
 template <class E, int kCtas>
 int launch_split(const ArgmaxArgs& a, int threads, cudaStream_t stream) {
   // kCtas CTAs per row, up to 2^30 CTAs; rows beyond that are taken in a grid-stride loop
@@ -385,28 +353,18 @@ int launch_argmax(const void* logits, int64_t rows, int64_t vocab, int64_t strid
   a.stride = stride;
   a.vec = aligned16(logits) && (stride * sizeof(S)) % 16 == 0 && (vocab * sizeof(S)) % 16 == 0;
 
-  // Many rows: a CTA per row, several per SM, each thread streaming several chunks. Fewer
-  // rows: the split (1, 2, 4 or 8 CTAs per row) and CTA size with the fewest chunk rounds; on a
-  // tie, the one with the most threads (the most SMs at work), then the smaller split (fewer
-  // cluster barriers).
-  if (rows >= 2 * static_cast<int64_t>(sm_count(device))) {
-    return launch_split<E, 1>(a, kMinThreads, stream);
-  }
-  const Shape shapes[4] = {shape_for<E, 1>(a, device), shape_for<E, 2>(a, device),
-                           shape_for<E, 4>(a, device), shape_for<E, kMaxCtasPerRow>(a, device)};
-  int pick = 0;
-  for (int k = 1; k < 4; ++k) {
-    const Shape& c = shapes[k];
-    const Shape& p = shapes[pick];
-    const int64_t c_threads = (rows << k) * c.threads, p_threads = (rows << pick) * p.threads;
-    if (c.rounds < p.rounds || (c.rounds == p.rounds && c_threads > p_threads)) pick = k;
-  }
-  switch (pick) {
-    case 0: return launch_split<E, 1>(a, shapes[0].threads, stream);
-    case 1: return launch_split<E, 2>(a, shapes[1].threads, stream);
-    case 2: return launch_split<E, 4>(a, shapes[2].threads, stream);
-    default: return launch_split<E, kMaxCtasPerRow>(a, shapes[3].threads, stream);
-  }
+  // Launch shapes from a sweep of every (CTAs per row, threads per CTA) in {1, 2, 4, 8} x
+  // {256, 512, 1024} on a B200 (148 SMs) at 1 to 2048 rows of 151,936 bf16 logits: one CTA per
+  // row wins from SMs/2 rows up (512 threads below 2 * SMs rows, 256 above, where the grid runs
+  // in several waves); below that a row is split over a cluster, 4 x 256 threads down to SMs/4
+  // rows and 8 x 512 under it (a single row: 5.2 us, about a kernel launch and one L2 round
+  // trip). A split whose CTAs do not all fit on the GPU at once loses: each cluster is scheduled
+  // whole.
+  const int64_t sms = sm_count(device);
+  if (rows >= 2 * sms) return launch_split<E, 1>(a, 256, stream);
+  if (2 * rows >= sms) return launch_split<E, 1>(a, 512, stream);
+  if (4 * rows >= sms) return launch_split<E, 4>(a, 256, stream);
+  return launch_split<E, kMaxCtasPerRow>(a, 512, stream);
 }
 
 }  // namespace
