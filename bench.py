@@ -796,11 +796,15 @@ def validate(chain, inp, cfg, world, rank, dev, rows: int = 256):
         bv = want[name].float().numpy()
         flat_b = np.abs(bv).reshape(bv.shape[0], -1).max(axis=1)
         tol = (2.0 ** -7 * flat_b).reshape((-1,) + (1,) * (bv.ndim - 1))
+        # a rotation output that cancels to near zero can be many ulps off in its own scale and
+        # still within one rounding of the terms it came from: held to 2^-7 of the row's largest
         within = (ulp <= 2) | (np.abs(av - bv) <= tol)
         exact_needed = name in ("embedding", "residual")
         good = bool((ulp == 0).all()) if exact_needed else bool(within.all())
         ok = ok and good
+        scale = np.maximum(flat_b, np.finfo(np.float32).tiny).reshape(tol.shape)
         report[name] = {"worst_bf16_ulp": int(ulp.max()), "not_bit_exact": int((ulp > 0).sum()),
+                        "worst_abs_err_over_row_max": float((np.abs(av - bv) / scale).max()),
                         "ok": good}
     return {"rows_per_gpu": n, "gathered_from": world, "against": "svllm_ops CPU backend",
             "ops": report, "ok": ok}

@@ -150,6 +150,9 @@ __device__ __forceinline__ int64_t load_slot(const RopeArgs& a, int64_t t) {
   return __ldg(reinterpret_cast<const long long*>(a.slots) + t);
 }
 
+// 16-byte vectors of a token's v row each lane holds in registers (a 2 KB row per warp).
+constexpr int kVRegs = 4;
+
 template <class E, int G, bool kNorm, bool kCache>
 __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ RopeArgs a) {
   using S = typename E::Storage;
@@ -204,14 +207,10 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
     const int s = static_cast<int>(j % a.stages);
     uint8_t* st = ring + static_cast<size_t>(s) * a.stage_bytes;
     const int64_t t = wu.at(j);
-    mbar_arrive_expect_tx(&bars[s], q_bytes + k_bytes + v_bytes);
+    mbar_arrive_expect_tx(&bars[s], q_bytes + k_bytes);
     if (q_bytes) bulk_load(st, static_cast<const uint8_t*>(a.q) + t * q_stride_b, q_bytes, &bars[s]);
     if (k_bytes) {
       bulk_load(st + q_bytes, static_cast<const uint8_t*>(a.k) + t * k_stride_b, k_bytes, &bars[s]);
-    }
-    if constexpr (kCache) {
-      bulk_load(st + q_bytes + k_bytes, static_cast<const uint8_t*>(a.v) + t * v_stride_b,
-                v_bytes, &bars[s]);
     }
   };
 
@@ -234,6 +233,19 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
       if (slot >= a.num_slots) {
         if (lane == 0) raise_error(a.err, kErrBadIndex);
         slot = -1;
+      }
+    }
+
+    // The token's v row goes to the cache unchanged: it is loaded into registers here (up to
+    // kVRegs vectors per lane) and stored after the heads, so it needs no shared memory and its
+    // load latency hides behind the token's work.
+    uint4 vr[kVRegs];
+    if constexpr (kCache) {
+      const uint8_t* vs = static_cast<const uint8_t*>(a.v) + wu.at(j) * v_stride_b;
+#pragma unroll
+      for (int r = 0; r < kVRegs; ++r) {
+        const uint32_t b = (lane + r * kWarpSize) * 16;
+        if (slot >= 0 && b < v_bytes) vr[r] = ld_global_nc_v4(vs + b);
       }
     }
 
@@ -302,11 +314,17 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
       }
     }
     if constexpr (kCache) {
-      if (slot >= 0) {  // v goes to the cache as it is
-        const uint8_t* vs = st + q_bytes + k_bytes;
+      if (slot >= 0) {
         uint8_t* vc = static_cast<uint8_t*>(a.v_cache) + slot * static_cast<int64_t>(v_bytes);
-        for (uint32_t b = lane * 16; b < v_bytes; b += kWarpSize * 16) {
-          st_global_v4(vc + b, ld_shared_v4(vs + b));
+#pragma unroll
+        for (int r = 0; r < kVRegs; ++r) {
+          const uint32_t b = (lane + r * kWarpSize) * 16;
+          if (b < v_bytes) st_global_v4(vc + b, vr[r]);
+        }
+        // rows longer than the registers hold: the rest copied directly
+        const uint8_t* vs = static_cast<const uint8_t*>(a.v) + wu.at(j) * v_stride_b;
+        for (uint32_t b = (lane + kVRegs * kWarpSize) * 16; b < v_bytes; b += kWarpSize * 16) {
+          st_global_v4(vc + b, ld_global_nc_v4(vs + b));
         }
       }
     }
@@ -530,7 +548,7 @@ int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
       bulk_ok ? pick_bulk_kernel<E, kNorm, kCache>(static_cast<int>(head_dim)) : nullptr;
   if (kernel != nullptr) {
     const PipelineShape shape = pipeline_shape(kNorm ? OpId::kQkNormRope : OpId::kRope);
-    a.stage_bytes = static_cast<int>(round_up(q_bytes + k_bytes + v_bytes, 128));
+    a.stage_bytes = static_cast<int>(round_up(q_bytes + k_bytes, 128));  // v is not staged
     int warps = warps_for(num_tokens, shape.warps, device);
     int stages = shape.stages;
     const int64_t half = head_dim / 2;
