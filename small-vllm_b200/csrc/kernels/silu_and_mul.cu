@@ -247,6 +247,11 @@ int launch_silu(void* out, const void* gate, const void* up, int64_t num_rows, i
     const PipelineShape shape = pipeline_shape(OpId::kSiluAndMul);
     constexpr int64_t kGranule = static_cast<int64_t>(kVec) * kWarpSize;  // one vector per lane
     int64_t chunk = shape.unit_bytes / (2 * static_cast<int64_t>(sizeof(S)));
+    // Small batches (decode): shrink the chunk until every SM has its tuned warp count of
+    // chunks, so that the SiLU arithmetic of a few thousand elements is spread over many warps
+    // instead of serialised in a few.
+    const int64_t want_units = static_cast<int64_t>(sm_count(device)) * shape.warps;
+    chunk = std::min<int64_t>(chunk, (a.rows * a.cols + want_units - 1) / want_units);
     chunk = std::max<int64_t>(kGranule, chunk / kGranule * kGranule);
     chunk = std::min<int64_t>(chunk, round_up(a.cols, kVec));
     a.chunk = chunk;

@@ -62,7 +62,9 @@ def _clear_device_error(cuda):
 # rms_norm
 
 RMS_SHAPES = [(1, 128), (4, 64), (7, 1024), (50, 2048), (3, 4100), (2, 16384), (300, 1024),
-              (4096, 128), (2049, 1024), (1000, 768), (33, 4096)]
+              (4096, 128), (2049, 1024), (1000, 768), (33, 4096),
+              # above 64 rows per SM: the bulk-copy kernels
+              (10000, 1024), (12000, 128), (10000, 2048), (10000, 768), (10000, 4096)]
 
 
 @pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
@@ -103,7 +105,7 @@ def test_rms_norm_strided_and_unaligned(cuda, dt):
 
 @pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
 @pytest.mark.parametrize("shape", [(1, 1024), (7, 1024), (1000, 1024), (513, 2048), (5, 4100),
-                                   (64, 128)], ids=str)
+                                   (64, 128), (10000, 1024), (10000, 2048), (12000, 128)], ids=str)
 def test_add_rms_norm(cuda, dt, shape):
     x = random_t(*shape, dtype=dt, device=cuda, seed=6)
     r = random_t(*shape, dtype=dt, device=cuda, seed=7)
@@ -306,14 +308,18 @@ def test_embedding_strided_output_rows(cuda):
 # ---------------------------------------------------------------------------------------------
 # pipeline shapes do not change results
 
+# the library's built-in shapes (host_common.cu), restored after each override
+DEFAULT_SHAPES = {"rms_norm": (8192, 2, 8), "silu_and_mul": (8192, 2, 6)}
+
+
 @pytest.mark.parametrize("unit, stages, warps", [(2048, 2, 1), (4096, 3, 8), (16384, 4, 2)])
 def test_pipeline_shape_does_not_change_results(cuda, unit, stages, warps):
-    x = random_t(999, 1024, device=cuda, seed=24)
+    x = random_t(12000, 1024, device=cuda, seed=24)  # enough rows for the bulk-copy kernel
     w = random_t(1024, device=cuda, seed=25)
     base = torch.empty_like(x)
     capi.rms_norm(base, x, w, 1e-6)
-    gate = random_t(50, 3072, device=cuda, seed=26)
-    up = random_t(50, 3072, device=cuda, seed=27)
+    gate = random_t(2000, 3072, device=cuda, seed=26)  # chunks of the tuned size, not shrunk
+    up = random_t(2000, 3072, device=cuda, seed=27)
     sbase = torch.empty_like(gate)
     capi.silu_and_mul(sbase, gate, up)
     try:
@@ -324,8 +330,8 @@ def test_pipeline_shape_does_not_change_results(cuda, unit, stages, warps):
         sout = torch.empty_like(gate)
         capi.silu_and_mul(sout, gate, up)
     finally:
-        for op in ("rms_norm", "silu_and_mul"):
-            capi.set_pipeline(op, 8192, 4, 4)
+        for op, shape in DEFAULT_SHAPES.items():
+            capi.set_pipeline(op, *shape)
     assert torch.equal(out, base) and torch.equal(sout, sbase)
 
 

@@ -23,7 +23,7 @@ SHAPES = [
     (2, 5, 2048),  # Llama 3.2 1B hidden size, batch and sequence dims flattened into rows
     (3, 4100),  # not a multiple of 8: the plain-load path
     (2, 16384),  # a row longer than the bulk path holds in registers: the plain-load path
-    (300, 1024),  # more rows than one CTA's warps: several pipeline stages per warp
+    (300, 1024),  # several rows per CTA of the row-block kernel's grid
 ]
 
 
@@ -76,10 +76,17 @@ def test_module_attributes():
     assert svllm_ops.built_with_cuda is True
 
 
+# Up to 64 rows per SM (9472 on a B200) the row-block kernel runs; above, the bulk-copy kernels,
+# one per row width: both must equal the reference kernel bit for bit.
+BULK_SHAPES = [(10000, 1024), (12000, 128), (10000, 64), (10000, 768), (10000, 2048),
+               (10000, 4096), (10000, 96)]
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("shape", [s for s in SHAPES if s[0]] + [(4096, 1024), (256 * 16, 128),
                                                                   (1000, 768), (50, 4096),
-                                                                  (9, 6144), (70, 96)], ids=str)
+                                                                  (9, 6144), (70, 96)]
+                         + BULK_SHAPES, ids=str)
 def test_bit_identical_to_reference_cuda_kernel(cuda, shape):
     ref = oracle.reference_module()
     assert ref is not None, "oracle/_ref (the reference's kernels) was not built"
