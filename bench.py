@@ -30,6 +30,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path[:0] = [str(ROOT / "small-vllm_b200" / "python"), str(ROOT / "oracle")]
 
 METRIC = "fused layer-op achieved HBM GB/s (% of B200 peak) and tokens/s at 1/2/4/8 GPUs"
+NOMINAL_HBM_GBS = 8000.0  # B200 HBM3e, nominal
 UNIT = "GB/s"
 
 QWEN3 = dict(name="qwen3-0.6b", hidden=1024, heads=16, kv_heads=8, head_dim=128, inter=3072,
@@ -658,6 +659,10 @@ def main() -> int:
         torch.cuda.synchronize()
         del graph
     op_ms = {op: sum(a.elapsed_time(b) for a, b in ev[op]) / args.steps for op in names}
+    op_ms_median = {op: statistics.median(a.elapsed_time(b) for a, b in ev[op]) for op in names}
+    # ids repeat (T / V ~ 6.9 at 1M tokens), so the L2 can serve repeated table rows: the bytes
+    # of the distinct rows read, beside the algorithmic bytes, keep the embedding figure honest
+    unique_rows = int(torch.unique(inp["ids"]).numel()) if "embedding" in names else 0
 
     t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
     if world > 1:
@@ -702,6 +707,13 @@ def main() -> int:
             "frac_of_peak": round(value / (peak * world), 4),
             "ops_gbs_per_gpu": ops_gbs,
             "ops_ms_per_gpu": {op: round(op_ms[op], 4) for op in names},
+            "ops_ms_median_per_gpu": {op: round(op_ms_median[op], 4) for op in names},
+            "frac_of_nominal": round(value / (NOMINAL_HBM_GBS * world), 4),
+            "embedding_unique_rows": {
+                "rows": unique_rows, "of_tokens": T,
+                "gbs": round((unique_rows * 2 * cfg["hidden"] + T * (2 * cfg["hidden"] + 4))
+                             / (op_ms["embedding"] * 1e-3) / 1e9, 1)}
+            if "embedding" in names else None,
             "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic,
@@ -910,9 +922,49 @@ def measure_e2e(chain, inp, cfg, args, world, dev):
         dist.all_reduce(tt)
         total = int(tt.item())
     value = sum(op_bytes(cfg).values()) * total / (ms * 1e-3) / 1e9
+    bound = pcie_bound_ms(dev, h2d, d2h)
     return {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d * world,
             "d2h_bytes_per_step": d2h * world, "ms_per_step": round(ms, 3),
-            "chunks": chunks, "api": "svllm_ops (pinned host buffers, 3 streams)"}
+            "chunks": chunks, "api": "svllm_ops (pinned host buffers, 3 streams)",
+            "pcie": {**bound, "frac": round(bound["bound_ms"] / ms, 4)}}
+
+
+def pcie_bound_ms(dev, h2d: int, d2h: int) -> dict:
+    """The step time PCIe alone allows: pinned-buffer copies measured here, one direction alone
+    and both at once; the copy-out overlaps the copy-in at the two-way rate, the rest of the
+    larger direction runs at the one-way rate."""
+    import torch
+
+    n = 1 << 29
+    hs = [torch.empty(n, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+    ds = [torch.empty(n, dtype=torch.uint8, device=dev) for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def timed(fn) -> float:
+        fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        return (time.perf_counter() - t0) / 3
+
+    def one_way():
+        with torch.cuda.stream(s_in):
+            ds[0].copy_(hs[0], non_blocking=True)
+
+    def two_way():
+        with torch.cuda.stream(s_in):
+            ds[0].copy_(hs[0], non_blocking=True)
+        with torch.cuda.stream(s_out):
+            hs[1].copy_(ds[1], non_blocking=True)
+
+    one = n / timed(one_way)
+    both = n / timed(two_way)
+    small, large = sorted((h2d, d2h))
+    bound_s = small / both + (large - small) / one
+    return {"one_way_gbs": round(one / 1e9, 1), "two_way_gbs_each": round(both / 1e9, 1),
+            "bound_ms": round(bound_s * 1e3, 1)}
 
 
 if __name__ == "__main__":
