@@ -15,8 +15,6 @@ __device__ int g_library_error_word = 0;
 
 namespace {
 
-constexpr int kMaxDevices = 64;
-
 std::atomic<int> g_sm_count[kMaxDevices];
 std::atomic<int*> g_error_word[kMaxDevices];
 

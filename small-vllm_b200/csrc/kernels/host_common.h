@@ -23,6 +23,9 @@ enum class OpId { kRmsNorm, kAddRmsNorm, kQkNormRope, kRope, kSiluAndMul, kEmbed
 PipelineShape pipeline_shape(OpId op);
 int set_pipeline_shape(const char* op, int64_t unit_bytes, int64_t stages, int64_t warps);
 
+// Devices the per-device caches hold (current_device rejects higher ordinals).
+constexpr int kMaxDevices = 64;
+
 // The current device and its SM count (cached per device).
 int current_device(int* device);
 int sm_count(int device);

@@ -11,17 +11,19 @@
 //     otherwise (gate and up as the two halves of one [rows, 2 * inter] tensor, say) chunks stay
 //     inside a row. Each warp owns a ring of stages; lane 0 keeps cp.async.bulk loads of the
 //     next chunks of gate and up in flight, and the warp writes 16-byte vectors of out.
-//   * Table path (bf16, large batches): a bf16 gate takes only 65536 values, so round(silu(g))
-//     is a function of the gate's 16 bits. Each CTA first evaluates that function for every
-//     bf16 pattern with the same expf / IEEE-division code into a 128 KB shared-memory table,
-//     then the stream needs one table load and one packed bf16 multiply per element instead of
-//     ~30 instructions of accurate math: identical results, a fraction of the issue slots. The
-//     table costs 65536 evaluations per CTA, so it is used only when every CTA has many times
-//     that many elements to process.
+//   * Table path (bf16, larger batches): a bf16 gate takes only 65536 values, so
+//     round(silu(g)) is a function of the gate's 16 bits. A one-time kernel per device evaluates
+//     it for every bf16 pattern, with the same expf / IEEE-division code, into a 128 KB table in
+//     device memory and then publishes it (a release store of a ready flag). Each CTA of a
+//     table-path launch copies the published table into shared memory, then streams with one
+//     table load and one packed bf16 multiply per element instead of ~30 instructions of
+//     accurate math: identical results, a fraction of the issue slots. A CTA that finds the
+//     table not yet published (the build still queued on another stream) computes directly.
 //   * Plain path for unaligned or odd-sized rows: grid-stride element loop, still on the GPU.
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 
 #include "common.cuh"
@@ -51,6 +53,19 @@ struct SiluArgs {
 
 constexpr int kTableEntries = 65536;  // one per bf16 bit pattern
 constexpr int kTableBytes = kTableEntries * 2;
+// The table path from this many elements per SM (measured on a B200 at 3072 columns: direct
+// math wins at 1024 tokens, 21k elements per SM, 7.5 us; the table at 2048 tokens, 10.1 us
+// against 11.9 us direct at 1536; from 4096 tokens on it saves 25-40%).
+constexpr int64_t kTableMinElementsPerSm = 24576;
+
+// round(silu(g)) for every bf16 pattern g, two per word (low half: the even pattern), built
+// once per device by silu_table_build_kernel; g_silu_table_ready turns 1 when it is complete.
+// Read-only after that; it never changes, so every launch on every stream may share it.
+__device__ __align__(256) uint32_t g_silu_table[kTableEntries / 2];
+__device__ int g_silu_table_ready = 0;
+
+// Whether the table build has been enqueued on each device (host side).
+std::atomic<bool> g_silu_table_launched[kMaxDevices];
 
 __device__ __forceinline__ float silu(float g) {
   return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
@@ -95,6 +110,30 @@ __device__ __forceinline__ uint4 silu_mul_vec_table(const uint4& g, const uint4&
   return make_uint4(y[0], y[1], y[2], y[3]);
 }
 
+__device__ __forceinline__ uint32_t silu_table_word(int w) {
+  const float g0 = __uint_as_float(static_cast<uint32_t>(2 * w) << 16);
+  const float g1 = __uint_as_float(static_cast<uint32_t>(2 * w + 1) << 16);
+  return pack_bf16x2(silu(g0), silu(g1));
+}
+
+__global__ void __launch_bounds__(1024) silu_table_build_kernel() {
+  for (int w = threadIdx.x; w < kTableEntries / 2; w += blockDim.x) {
+    g_silu_table[w] = silu_table_word(w);
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(&g_silu_table_ready), "r"(1)
+                 : "memory");
+  }
+}
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 template <class E, bool kTable>
 __global__ void __launch_bounds__(512) silu_bulk_kernel(const SiluArgs a) {
   using S = typename E::Storage;
@@ -114,15 +153,31 @@ __global__ void __launch_bounds__(512) silu_bulk_kernel(const SiluArgs a) {
     for (int s = 0; s < a.stages; ++s) mbar_init(&bars[s], 1);
     fence_mbar_init();
   }
+  __shared__ int ready;
+  __shared__ __align__(8) uint64_t table_bar;
+  bool use_table = false;
+  bool table_copy_pending = false;  // a table copy this CTA must see land before it exits
   if constexpr (kTable) {
-    // round(silu(g)) for every bf16 pattern g, two per 32-bit word
-    uint32_t* table_words = reinterpret_cast<uint32_t*>(smem + a.table_offset);
-    for (int w = threadIdx.x; w < kTableEntries / 2; w += blockDim.x) {
-      const float g0 = __uint_as_float(static_cast<uint32_t>(2 * w) << 16);
-      const float g1 = __uint_as_float(static_cast<uint32_t>(2 * w + 1) << 16);
-      table_words[w] = pack_bf16x2(silu(g0), silu(g1));
+    // The published table, one bulk copy into shared memory; before it is published, direct
+    // math.
+    if (threadIdx.x == 0) {
+      ready = ld_acquire_gpu(&g_silu_table_ready);
+      if (ready) {
+        mbar_init(&table_bar, 1);
+        fence_mbar_init();
+        // the table's generic-proxy writes, acquired above, ordered before the async-proxy read
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        mbar_arrive_expect_tx(&table_bar, kTableBytes);
+        bulk_load(smem + a.table_offset, g_silu_table, kTableBytes, &table_bar);
+      }
     }
     __syncthreads();
+    use_table = ready != 0 && __syncthreads_and(mbar_wait_bounded(&table_bar, 0));
+    if (ready && !use_table) {
+      // the copy did not land in time: direct math, and the copy is waited for before exit
+      table_copy_pending = true;
+      if (threadIdx.x == 0) raise_error(a.err, kErrWaitTimeout);
+    }
   } else {
     __syncwarp();
   }
@@ -171,7 +226,7 @@ __global__ void __launch_bounds__(512) silu_bulk_kernel(const SiluArgs a) {
     for (int v = lane; v < nv; v += kWarpSize) {
       const uint4 g = ld_shared_v4(st + v * 16);
       const uint4 u = ld_shared_v4(st + half_stage + v * 16);
-      if constexpr (kTable) {
+      if (kTable && use_table) {
         st_global_v4(out + v * kVec, silu_mul_vec_table(g, u, table));
       } else {
         st_global_v4(out + v * kVec, silu_mul_vec<E>(g, u));
@@ -192,6 +247,9 @@ __global__ void __launch_bounds__(512) silu_bulk_kernel(const SiluArgs a) {
       }
     }
     __syncwarp();
+  }
+  if constexpr (kTable) {
+    if (threadIdx.x == 0 && table_copy_pending) mbar_wait_bounded(&table_bar, 0);
   }
 }
 
@@ -256,9 +314,18 @@ int launch_silu(void* out, const void* gate, const void* up, int64_t num_rows, i
     chunk = std::min<int64_t>(chunk, round_up(a.cols, kVec));
     a.chunk = chunk;
     a.stage_bytes = static_cast<int>(round_up(2 * chunk * static_cast<int64_t>(sizeof(S)), 128));
-    // The table pays for itself once every CTA has many times 65536 elements to process.
     const bool table = sizeof(S) == 2 &&
-                       a.rows * a.cols >= static_cast<int64_t>(sm_count(device)) * 4 * kTableEntries;
+                       a.rows * a.cols >= static_cast<int64_t>(sm_count(device)) *
+                                              kTableMinElementsPerSm;
+    if (table && !g_silu_table_launched[device].exchange(true)) {
+      // once per device, on the caller's stream: calls after it on this stream find the table
+      // published; calls racing it on other streams compute directly until it is
+      silu_table_build_kernel<<<1, 1024, 0, stream>>>();
+      if (cudaGetLastError() != cudaSuccess) {
+        g_silu_table_launched[device].store(false);
+        return SVLLM_ERR_LAUNCH;
+      }
+    }
     const int64_t table_bytes = table ? kTableBytes : 0;
     int warps = warps_for(a.rows * ((a.cols + chunk - 1) / chunk), shape.warps, device);
     int stages = shape.stages;
