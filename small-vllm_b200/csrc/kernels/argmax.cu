@@ -269,6 +269,7 @@ __device__ __forceinline__ int64_t ld_cluster_s64(uint32_t addr) {
 // cluster runs the same rows, so all meet every cluster barrier.
 template <class E, int kCtas>
 __global__ void __launch_bounds__(kMaxThreads) argmax_kernel(const ArgmaxArgs a) {
+  grid_dependency_sync();
   using S = typename E::Storage;
   __shared__ float red_v[kMaxThreads / kWarpSize];
   __shared__ int64_t red_i[kMaxThreads / kWarpSize];
@@ -316,21 +317,8 @@ int launch_split(const ArgmaxArgs& a, int threads, cudaStream_t stream) {
   // kCtas CTAs per row, up to 2^30 CTAs; rows beyond that are taken in a grid-stride loop
   constexpr int64_t kMaxGroups = (int64_t{1} << 30) / kCtas;
   const int64_t groups = a.rows < kMaxGroups ? a.rows : kMaxGroups;
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(groups * kCtas));
-  cfg.blockDim = dim3(static_cast<unsigned>(threads));
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kCtas;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = kCtas > 1 ? 1 : 0;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, argmax_kernel<E, kCtas>, a);
-  const int status = launch_status();  // also clears the error a failed launch leaves
-  return err == cudaSuccess ? status : SVLLM_ERR_LAUNCH;
+  return launch(argmax_kernel<E, kCtas>, dim3(static_cast<unsigned>(groups * kCtas)),
+                dim3(static_cast<unsigned>(threads)), 0, stream, kCtas, a);
 }
 
 template <class E>

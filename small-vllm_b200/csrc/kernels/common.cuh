@@ -209,6 +209,14 @@ __device__ __forceinline__ uint4 ld_shared_v4(const void* p) {
 // mbarrier + bulk copy (cp.async.bulk, the non-tensor TMA path). No .multicast::cluster form is
 // used anywhere in this library: every copy moves this GPU's own memory into its own CTA.
 
+// Programmatic dependent launch: wait until the kernel before this one in the stream has
+// completed and its memory is visible (a no-op when launched without the attribute), then let
+// the next kernel be scheduled. Every kernel runs this first, before any memory access.
+__device__ __forceinline__ void grid_dependency_sync() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -47,6 +47,7 @@ __device__ __forceinline__ int64_t load_id(const void* ids, int is_i64, int64_t 
 }
 
 __global__ void __launch_bounds__(512) embedding_bulk_kernel(const EmbArgs a) {
+  grid_dependency_sync();
   extern __shared__ __align__(128) uint8_t smem[];
   const int warps = blockDim.x / kWarpSize;
   const int warp = threadIdx.x / kWarpSize;
@@ -136,6 +137,7 @@ __global__ void __launch_bounds__(512) embedding_bulk_kernel(const EmbArgs a) {
 }
 
 __global__ void __launch_bounds__(256) embedding_plain_kernel(const EmbArgs a) {
+  grid_dependency_sync();
   const int lane = threadIdx.x % kWarpSize;
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x / kWarpSize);
   const int64_t elems = a.row_bytes / a.elem_bytes;
@@ -210,15 +212,15 @@ int launch_embedding(void* out, const void* ids, int id_type, const void* table,
                                        threads, smem, device);
       if (per_sm > 0) {
         const int64_t grid = persistent_grid((num_tokens + warps - 1) / warps, device, per_sm);
-        embedding_bulk_kernel<<<static_cast<unsigned>(grid), threads, smem, stream>>>(a);
-        return launch_status();
+        return launch(embedding_bulk_kernel, dim3(static_cast<unsigned>(grid)), dim3(threads),
+                      smem, stream, 1, a);
       }
     }
   }
 
   const int64_t grid = persistent_grid((num_tokens + 7) / 8, device, 8);
-  embedding_plain_kernel<<<static_cast<unsigned>(grid), 256, 0, stream>>>(a);
-  return launch_status();
+  return launch(embedding_plain_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0, stream, 1,
+                a);
 }
 
 }  // namespace

@@ -6,6 +6,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <utility>
 
 #include "svllm_kernels.h"
 
@@ -56,6 +57,33 @@ inline int launch_status() {
 inline int warps_for(int64_t units, int tuned, int device) {
   const int64_t per_sm = (units + sm_count(device) - 1) / sm_count(device);
   return static_cast<int>(per_sm < tuned ? (per_sm > 0 ? per_sm : 1) : tuned);
+}
+
+// Launches `kernel` with programmatic dependent launch allowed: the grid may be scheduled
+// while the kernel before it in the stream is still running, and every kernel of this library
+// waits (griddepcontrol.wait, its first statement) until that kernel has completed and its
+// memory is visible before touching any. What it hides is the gap between kernels: launch
+// processing and CTA start-up. `cluster` > 1 also sets the cluster size.
+template <class... Params, class... Args>
+int launch(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+           unsigned cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = cluster > 1 ? 2 : 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  const int status = launch_status();  // also clears the error a failed launch leaves
+  return err == cudaSuccess ? status : SVLLM_ERR_LAUNCH;
 }
 
 // Grid size for a persistent kernel: enough CTAs to fill every SM at the given occupancy, but

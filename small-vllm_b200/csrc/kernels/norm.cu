@@ -77,6 +77,7 @@ __device__ __forceinline__ void load_rows(uint8_t* dst, const void* base, int64_
 
 template <class E, int G, int V, bool kAdd>
 __global__ void __launch_bounds__(512) norm_bulk_kernel(const NormArgs a) {
+  grid_dependency_sync();
   using S = typename E::Storage;
   constexpr int kVec = E::kPerVec;
   constexpr int kRowsPerPass = kWarpSize / G;
@@ -222,6 +223,7 @@ __global__ void __launch_bounds__(512) norm_bulk_kernel(const NormArgs a) {
 // thread-to-element mapping and reduction tree.
 template <class E, int N, bool kAdd>
 __global__ void __launch_bounds__(1024) norm_rowblock_kernel(const NormArgs a) {
+  grid_dependency_sync();
   using S = typename E::Storage;
   struct alignas(sizeof(S) * N) Pack {
     S v[N];
@@ -381,8 +383,8 @@ int launch_norm(void* out, const void* x, void* residual, const void* weight, in
         if (per_sm > 0) {
           const int64_t num_units = (num_rows + rows - 1) / rows;
           const int64_t grid = persistent_grid((num_units + warps - 1) / warps, device, per_sm);
-          kernel<<<static_cast<unsigned>(grid), threads, smem, stream>>>(a);
-          return launch_status();
+          return launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1,
+                        a);
         }
       }
     }
@@ -399,8 +401,7 @@ int launch_norm(void* out, const void* x, void* residual, const void* weight, in
   const auto kernel = vec ? norm_rowblock_kernel<E, kVec, kAdd> : norm_rowblock_kernel<E, 1, kAdd>;
   const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(kernel), threads, 0, device);
   const int64_t grid = persistent_grid(num_rows, device, per_sm > 0 ? per_sm : 1);
-  kernel<<<static_cast<unsigned>(grid), threads, 0, stream>>>(a);
-  return launch_status();
+  return launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(threads), 0, stream, 1, a);
 }
 
 }  // namespace

@@ -155,6 +155,7 @@ constexpr int kVRegs = 4;
 
 template <class E, int G, bool kNorm, bool kCache>
 __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ RopeArgs a) {
+  grid_dependency_sync();
   using S = typename E::Storage;
   constexpr int kVec = E::kPerVec;
   constexpr int kHalf = kVec * G;  // head_dim / 2
@@ -378,6 +379,7 @@ __device__ float reference_order_inv_rms(const typename E::Storage* x, int n, fl
 // Plain path: one warp per token, any head_dim (even), any alignment.
 template <class E, bool kNorm, bool kCache>
 __global__ void __launch_bounds__(256) rope_plain_kernel(const __grid_constant__ RopeArgs a) {
+  grid_dependency_sync();
   using S = typename E::Storage;
   const int lane = threadIdx.x % kWarpSize;
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x / kWarpSize);
@@ -570,15 +572,15 @@ int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
       const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(kernel), threads, smem, device);
       if (per_sm > 0) {
         const int64_t grid = persistent_grid((num_tokens + warps - 1) / warps, device, per_sm);
-        kernel<<<static_cast<unsigned>(grid), threads, smem, stream>>>(a);
-        return launch_status();
+        return launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1,
+                      a);
       }
     }
   }
 
   const int64_t grid = persistent_grid((num_tokens + 7) / 8, device, 8);
-  rope_plain_kernel<E, kNorm, kCache><<<static_cast<unsigned>(grid), 256, 0, stream>>>(a);
-  return launch_status();
+  return launch(rope_plain_kernel<E, kNorm, kCache>, dim3(static_cast<unsigned>(grid)), dim3(256),
+                0, stream, 1, a);
 }
 
 }  // namespace

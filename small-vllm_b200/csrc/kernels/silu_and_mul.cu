@@ -117,6 +117,7 @@ __device__ __forceinline__ uint32_t silu_table_word(int w) {
 }
 
 __global__ void __launch_bounds__(1024) silu_table_build_kernel() {
+  grid_dependency_sync();
   for (int w = threadIdx.x; w < kTableEntries / 2; w += blockDim.x) {
     g_silu_table[w] = silu_table_word(w);
   }
@@ -136,6 +137,7 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
 
 template <class E, bool kTable>
 __global__ void __launch_bounds__(512) silu_bulk_kernel(const SiluArgs a) {
+  grid_dependency_sync();
   using S = typename E::Storage;
   constexpr int kVec = E::kPerVec;
   static_assert(!kTable || sizeof(S) == 2, "the table path is for bf16");
@@ -255,6 +257,7 @@ __global__ void __launch_bounds__(512) silu_bulk_kernel(const SiluArgs a) {
 
 template <class E>
 __global__ void __launch_bounds__(256) silu_plain_kernel(const SiluArgs a) {
+  grid_dependency_sync();
   using S = typename E::Storage;
   const int64_t total = a.rows * a.cols;
   const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -320,8 +323,7 @@ int launch_silu(void* out, const void* gate, const void* up, int64_t num_rows, i
     if (table && !g_silu_table_launched[device].exchange(true)) {
       // once per device, on the caller's stream: calls after it on this stream find the table
       // published; calls racing it on other streams compute directly until it is
-      silu_table_build_kernel<<<1, 1024, 0, stream>>>();
-      if (cudaGetLastError() != cudaSuccess) {
+      if (launch(silu_table_build_kernel, dim3(1), dim3(1024), 0, stream, 1) != SVLLM_OK) {
         g_silu_table_launched[device].store(false);
         return SVLLM_ERR_LAUNCH;
       }
@@ -346,15 +348,15 @@ int launch_silu(void* out, const void* gate, const void* up, int64_t num_rows, i
       if (per_sm > 0) {
         const int64_t units = a.rows * ((a.cols + chunk - 1) / chunk);
         const int64_t grid = persistent_grid((units + warps - 1) / warps, device, per_sm);
-        kernel<<<static_cast<unsigned>(grid), threads, smem, stream>>>(a);
-        return launch_status();
+        return launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1,
+                      a);
       }
     }
   }
 
   const int64_t grid = persistent_grid((a.rows * a.cols + 255) / 256, device, 8);
-  silu_plain_kernel<E><<<static_cast<unsigned>(grid), 256, 0, stream>>>(a);
-  return launch_status();
+  return launch(silu_plain_kernel<E>, dim3(static_cast<unsigned>(grid)), dim3(256), 0, stream, 1,
+                a);
 }
 
 }  // namespace
