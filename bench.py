@@ -35,8 +35,8 @@ UNIT = "GB/s"
 
 QWEN3 = dict(name="qwen3-0.6b", hidden=1024, heads=16, kv_heads=8, head_dim=128, inter=3072,
              vocab=151936, eps=1e-6, theta=1e6, qk_norm=True, scaling=None)
-# Llama-3.2-1B; the benchmark definition states llama3 scaling factor 32 (the model's config.json
-# has 8.0; the formula is the same and both are tested)
+# Llama-3.2-1B with llama3 rope scaling at factor 32 (the model's config.json has 8.0; the
+# formula is the same and both are tested)
 LLAMA = dict(name="llama-3.2-1b", hidden=2048, heads=32, kv_heads=8, head_dim=64, inter=8192,
              vocab=128256, eps=1e-5, theta=5e5, qk_norm=False, scaling=(32.0, 1.0, 4.0, 8192))
 

@@ -116,7 +116,7 @@ def assert_bf16_within_ulp(actual, expected, max_ulp: int, what: str = "") -> fl
 
 
 def assert_rel_f32(actual, expected, rtol: float = 1e-5, what: str = "", scale=None) -> None:
-    """fp32: |a - e| <= rtol * max(|e|, s) per element (the north star's 1e-5 relative bar),
+    """fp32: |a - e| <= rtol * max(|e|, s) per element (the fp32 ops' 1e-5 relative bar),
     where s is the magnitude the element was computed from: by default the RMS of its row (the
     last axis), so a value that cancels to near zero is held to the row's scale, not its own."""
     a = np.asarray(to_bits(actual), dtype=np.float64)

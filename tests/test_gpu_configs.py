@@ -1,12 +1,13 @@
-"""The five workloads of the benchmark definition, end to end through svllm_ops on the GPU.
+"""Five whole workloads, end to end through svllm_ops on the GPU.
 
-  config 0  Qwen3 shapes, fp32, T=256 (through the C ABI's fp32 entry points: svllm_ops is bf16
-            only, like the reference) against the C/OpenMP oracle, 1e-5 relative.
-  config 1  Qwen3 decode, bf16, 256 single-token sequences, positions uniform in [0, 4096).
-  config 2  Qwen3 packed prefill, 64 sequences of uniform [128, 2048] tokens, positions 0..len-1.
-  config 3  Llama-3.2-1B shapes, T=16384 = 8 x 2048, llama3 rope scaling at factor 32 (as the
-            benchmark states it) and 8 (the model's config.json).
-  config 4  the 1,048,576-token bandwidth sweep at full size.
+  fp32       Qwen3 shapes, fp32, T=256 (through the C ABI's fp32 entry points: svllm_ops is bf16
+             only, like the reference) against the C/OpenMP oracle, 1e-5 relative.
+  decode     Qwen3, bf16, 256 single-token sequences, positions uniform in [0, 4096).
+  prefill    Qwen3 packed prefill, 64 sequences of uniform [128, 2048] tokens, positions
+             0..len-1.
+  llama      Llama-3.2-1B shapes, T=16384 = 8 x 2048, llama3 rope scaling at factor 32 and 8
+             (the model's config.json).
+  sweep      the 1,048,576-token bandwidth sweep at full size.
 
 At full size the bf16 checks are the size-independent ones: bit-identity with the reference's own
 rms_norm kernel (oracle/_ref) on the same GPU, bit-identity with the torch composites that call
@@ -126,7 +127,7 @@ def check_chain_bf16(inp, cfg, qk_norm=True, scaling=None, sample_rows=512):
     assert_bf16_within_ulp(y[rows], oy, 2, "silu_and_mul vs oracle")
 
 
-def test_config0_qwen3_fp32_t256(cuda):
+def test_qwen3_fp32_t256(cuda):
     cfg, T = QWEN, 256
     g = torch.Generator().manual_seed(0)
     f = lambda *s, scale=1.0, shift=0.0: (torch.randn(s, generator=g) * scale + shift)  # noqa
@@ -168,12 +169,12 @@ def test_config0_qwen3_fp32_t256(cuda):
     assert_rel_f32(y, oy, 1e-5, "silu")
 
 
-def test_config1_qwen3_decode(cuda):
+def test_qwen3_decode(cuda):
     inp = make(QWEN, 256, cuda, seed=1, pos_hi=4096)
     check_chain_bf16(inp, QWEN)
 
 
-def test_config2_qwen3_packed_prefill(cuda):
+def test_qwen3_packed_prefill(cuda):
     g = torch.Generator().manual_seed(2)
     lens = torch.randint(128, 2049, (64,), generator=g)
     pos = torch.cat([torch.arange(int(n)) for n in lens]).to(cuda)
@@ -182,13 +183,13 @@ def test_config2_qwen3_packed_prefill(cuda):
 
 
 @pytest.mark.parametrize("factor", [32.0, 8.0])
-def test_config3_llama_packed_batch(cuda, factor):
+def test_llama_packed_batch(cuda, factor):
     pos = torch.arange(2048, device=cuda).repeat(8)
     inp = make(LLAMA, 16384, cuda, seed=3, pos=pos)
     check_chain_bf16(inp, LLAMA, qk_norm=False, scaling=(factor, 1.0, 4.0, 8192))
 
 
-def test_config4_full_size_sweep(cuda):
+def test_full_size_sweep(cuda):
     inp = make(QWEN, 1 << 20, cuda, seed=4, pos_hi=32768)
     check_chain_bf16(inp, QWEN, sample_rows=2048)
     torch.cuda.synchronize()

@@ -2,7 +2,7 @@
 (oracle/, the C/OpenMP restatement) on the same seeded inputs, for bf16 and fp32, across the
 bulk-copy path, the plain-load path (unaligned or odd sizes), strided rows and the edge cases.
 
-Bars (the north star's tolerances, written per test):
+Bars (one bf16 ulp against the reference kernel, 1e-5 relative for fp32; written per test):
   * embedding: bit-exact.
   * fp32 outputs: within 1e-5 relative of the oracle.
   * bf16 norms: bit-identical to the reference's own CUDA rms_norm kernel (oracle/_ref, same

@@ -1,7 +1,7 @@
 """svllm_ops.rms_norm keeps the reference's contract: the reference's own op test
 (tests/python/test_rms_norm.py:9-66), same shapes, seeds, oracle, tolerance and error fragments,
 run on CPU and (marked gpu) on the sm_100a kernel. On CUDA it must also be bit-identical to the
-reference's own CUDA kernel, built from its sources for sm_100a (oracle/_ref): the north star
+reference's own CUDA kernel, built from its sources for sm_100a (oracle/_ref): the op's bar
 allows one bf16 ulp, and the kernels reproduce the reference's summation order and rsqrtf so
 that they need none."""
 
