@@ -341,15 +341,23 @@ int launch_argmax(const void* logits, int64_t rows, int64_t vocab, int64_t strid
   a.stride = stride;
   a.vec = aligned16(logits) && (stride * sizeof(S)) % 16 == 0 && (vocab * sizeof(S)) % 16 == 0;
 
-  // Launch shapes from a sweep of every (CTAs per row, threads per CTA) in {1, 2, 4, 8} x
-  // {256, 512, 1024} on a B200 (148 SMs) at 1 to 2048 rows of 151,936 bf16 logits: one CTA per
-  // row wins from SMs/2 rows up (512 threads below 2 * SMs rows, 256 above, where the grid runs
-  // in several waves); below that a row is split over a cluster, 4 x 256 threads down to SMs/4
-  // rows and 8 x 512 under it (a single row: 5.2 us, about a kernel launch and one L2 round
-  // trip). A split whose CTAs do not all fit on the GPU at once loses: each cluster is scheduled
-  // whole.
+  // Launch shapes from sweeps of (CTAs per row, threads per CTA) on a B200 (148 SMs) at 1 to
+  // 4096 rows of 151,936 bf16 logits. From 2 * SMs rows: one CTA per row, as large as lets every
+  // row's CTA be resident at once (a second, part-empty wave costs up to 13%: 600 rows take
+  // 32.8 us at 192 threads, 37.7 us at 256), else 128 threads. From SMs/2 rows: 512 threads.
+  // Fewer rows: a row is split over a cluster, 4 x 256 threads down to SMs/4 rows and 8 x 512
+  // under it (a single row: 5.2 us, about a kernel launch and one L2 round trip). A split whose
+  // CTAs do not all fit on the GPU at once loses: each cluster is scheduled whole.
   const int64_t sms = sm_count(device);
-  if (rows >= 2 * sms) return launch_split<E, 1>(a, 256, stream);
+  if (rows >= 2 * sms) {
+    const void* one = reinterpret_cast<const void*>(argmax_kernel<E, 1>);
+    for (const int threads : {256, 192, 128}) {
+      if (rows <= sms * blocks_per_sm(one, threads, 0, device)) {
+        return launch_split<E, 1>(a, threads, stream);
+      }
+    }
+    return launch_split<E, 1>(a, 128, stream);
+  }
   if (2 * rows >= sms) return launch_split<E, 1>(a, 512, stream);
   if (4 * rows >= sms) return launch_split<E, 4>(a, 256, stream);
   return launch_split<E, kMaxCtasPerRow>(a, 512, stream);

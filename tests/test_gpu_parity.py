@@ -487,10 +487,11 @@ def test_argmax_strided_rows_and_edge_values(cuda):
 
 @pytest.mark.parametrize("dt", DTYPES, ids=ids_of)
 @pytest.mark.parametrize("rows, vocab", [(4, 151936), (40, 151936), (100, 151936),
-                                         (200, 151937), (400, 151936)], ids=str)
+                                         (200, 151937), (400, 151936), (700, 151936),
+                                         (1100, 151936)], ids=str)
 def test_argmax_edge_rows_every_split(cuda, dt, rows, vocab):
-    """Row counts that give one row to 8 and 4 CTAs of a cluster, and to one CTA of 512 and of
-    256 threads (148 SMs); the odd vocabulary takes the element-wise path. Planted rows: every element tied, a row of -inf, ties across the
+    """Row counts that give one row to 8 and 4 CTAs of a cluster, and to one CTA of 512, 256,
+    192 and 128 threads (148 SMs); the odd vocabulary takes the element-wise path. Planted rows: every element tied, a row of -inf, ties across the
     slice boundaries of the CTAs sharing a row, a maximum in the last element, and NaNs after
     the maximum (the first NaN wins)."""
     logits = random_t(rows, vocab, dtype=dt, device=cuda, seed=62, scale=2.0)
