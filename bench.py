@@ -634,29 +634,26 @@ def main() -> int:
         for _ in range(args.steps):
             if graph is not None:
                 graph.replay()
-                continue
-            for op in names:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                chain.run_op(op)
-                e1.record(stream)
-                ev[op].append((e0, e1))
+            else:
+                for op in names:
+                    chain.run_op(op)
         stop.record(stream)
         torch.cuda.synchronize()
     barrier()
     elapsed_ms = start.elapsed_time(stop)
+    # Per-op times come from a second pass of the same steps with events around each launch
+    # (outside the timed region: events between kernels would stand in the way of the next
+    # kernel's early launch, and a graph replay has no per-op events).
+    for _ in range(args.steps):
+        for op in names:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            chain.run_op(op)
+            e1.record(stream)
+            ev[op].append((e0, e1))
+    torch.cuda.synchronize()
     if graph is not None:
-        # per-op times come from an eager pass of the same ops (a replay has no per-op events)
-        for _ in range(args.steps):
-            for op in names:
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                chain.run_op(op)
-                e1.record(stream)
-                ev[op].append((e0, e1))
-        torch.cuda.synchronize()
         del graph
     op_ms = {op: sum(a.elapsed_time(b) for a, b in ev[op]) / args.steps for op in names}
     op_ms_median = {op: statistics.median(a.elapsed_time(b) for a, b in ev[op]) for op in names}
