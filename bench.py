@@ -715,6 +715,8 @@ def main() -> int:
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic,
                          "algorithmic_bytes": nbytes[dominant] * T,
+                         "kernel_timing": "CUDA events around each launch, on the launching "
+                                          "stream, in a second pass of the same K steps",
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"
                          if not peaks.get("fallback") else "fallback 6650 GB/s"},
             "clocks": clocks,
