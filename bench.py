@@ -87,11 +87,13 @@ def parse_args():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=sorted(WORKLOADS) + ["sampling", "model-decode"],
+    p.add_argument("--workload",
+                   choices=sorted(WORKLOADS) + ["sampling", "lm-head", "model-decode"],
                    default="sweep",
                    help="sampling: greedy argmax over [tokens, 151936] bf16 logits (one op, "
-                        "not the chain); model-decode: Qwen3-0.6B decode steps through the "
-                        "model forward, eager and from CUDA graphs")
+                        "not the chain); lm-head: the tied LM head fused with greedy sampling "
+                        "(one tcgen05 kernel) beside matmul + argmax; model-decode: Qwen3-0.6B "
+                        "decode steps through the model forward, eager and from CUDA graphs")
     p.add_argument("--batches", default="1,8,64,256",
                    help="model-decode: comma-separated decode batch sizes")
     p.add_argument("--context", type=int, default=512,
@@ -466,6 +468,67 @@ def run_sampling(args) -> int:
     return 0
 
 
+def run_lm_head(args) -> int:
+    """The tied LM head fused with greedy sampling (svllm_ops.greedy_sample on CUDA: one tcgen05
+    GEMM whose epilogue takes the argmax) against torch.matmul + svllm_ops.argmax, at the
+    Qwen3-0.6B and Llama-3.2-1B vocabularies, decode to prefill batch sizes."""
+    import torch
+
+    import svllm_ops
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(11)
+    peaks = measured_peaks()
+    batches = [int(b) for b in args.batches.split(",")]
+
+    def replay_us(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(args.steps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        graph.replay()
+        stop.record()
+        torch.cuda.synchronize()
+        return start.elapsed_time(stop) / args.steps * 1e3
+
+    for cfg in (QWEN3, LLAMA):
+        v, h = cfg["vocab"], cfg["hidden"]
+        w = (torch.randn(v, h, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        for b in batches:
+            x = torch.randn(b, h, device=dev, generator=g).to(torch.bfloat16)
+            fused = replay_us(lambda: svllm_ops.greedy_sample(x, w))
+            split = replay_us(lambda: svllm_ops.argmax(torch.matmul(x, w.t())))
+            ids = svllm_ops.greedy_sample(x, w)
+            ref = torch.argmax(torch.matmul(x, w.t()), dim=-1)
+            weight_bytes = v * h * 2
+            flops = 2 * b * v * h
+            print(json.dumps({
+                "metric": "LM head + greedy sampling (fused tcgen05 GEMM + argmax)",
+                "value": round(fused, 2), "unit": "us", "n_gpus": 1, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(fused / 1e3, 5),
+                "higher_is_better": False, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "tied LM head + argmax", "model": cfg["name"],
+                           "batch": b, "vocab": v, "hidden": h,
+                           "timing": "CUDA graph replay of the steps"},
+                "matmul_then_argmax_us": round(split, 2), "speedup": round(split / fused, 3),
+                "weight_stream_gbs": round(weight_bytes / (fused * 1e-6) / 1e9, 1),
+                "weight_stream_frac_of_peak": round(weight_bytes / (fused * 1e-6) / 1e9
+                                                    / float(peaks["hbm_gbs"]), 4),
+                "tflops": round(flops / (fused * 1e-6) / 1e12, 1),
+                "tflops_frac_of_peak": round(flops / (fused * 1e-6) / 1e12
+                                             / float(peaks.get("bf16_tflops", 1590.0)), 4),
+                "ids_equal_to_matmul_argmax": round(float((ids == ref).float().mean()), 6),
+                "gpu_launches": 2 * args.steps}), flush=True)
+    return 0
+
+
 def model_weights(cfg: dict, layers: int, device, seed: int = 1234) -> dict:
     """Random Hugging Face-named weights of a Qwen3 model: projections N(0, 0.02), norm weights
     1 + N(0, 0.1), tied embedding."""
@@ -565,6 +628,8 @@ def main() -> int:
         return run_sampling(args)
     if args.workload == "model-decode":
         return run_model_decode(args)
+    if args.workload == "lm-head":
+        return run_lm_head(args)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)

@@ -229,14 +229,33 @@ int svllm_embedding_f32(float* out, const void* ids, int id_type, const float* t
  * Greedy sampling: out_ids[r] = argmax over logits[r, 0:vocab] (torch.argmax semantics: the
  * first index of the maximum, a NaN above every number). logits: [num_rows, vocab] at
  * row_stride elements, typically the tied-embedding LM head's output after the final norm
- * (src/model/config.h:28). out_ids: [num_rows] int64, device. A row is split over the 8 CTAs of
- * a thread-block cluster and reduced through distributed shared memory.
+ * (src/model/config.h:28). out_ids: [num_rows] int64, device. Few rows are split over the CTAs
+ * of a thread-block cluster and reduced through distributed shared memory.
  * New op (sampling on the GPU, docs/design-spec.md:28-29).
  */
 int svllm_argmax_bf16(const void* logits, int64_t num_rows, int64_t vocab, int64_t row_stride,
                       int64_t* out_ids, svllm_stream stream);
 int svllm_argmax_f32(const float* logits, int64_t num_rows, int64_t vocab, int64_t row_stride,
                      int64_t* out_ids, svllm_stream stream);
+
+/*
+ * Greedy sampling fused with the LM head: out_ids[r] = argmax over n of
+ * bf16(sum_k hidden[r, k] * weight[n, k]), the logits never written to memory (tcgen05 GEMM,
+ * fp32 accumulation, each logit rounded to bf16 as a bf16 matmul would store it, then
+ * torch.argmax semantics). hidden: [num_rows, hidden_size] bf16 at hidden_stride elements;
+ * weight: [vocab, hidden_size] bf16 at weight_stride elements (the tied embedding table,
+ * src/model/config.h:28); both 16-byte aligned with strides of whole 16 bytes, else
+ * SVLLM_ERR_UNSUPPORTED. logits: null, or a [num_rows, vocab] bf16 output at logits_stride
+ * elements that also receives the logits. workspace: at least 8 * num_rows bytes, 8-byte
+ * aligned, zero on entry and zero again when the call's work completes (so one zeroed buffer
+ * serves every call on a stream; calls that overlap on the GPU must not share it).
+ * New op (the LM head and sampling on the GPU, docs/design-spec.md:28-29).
+ */
+int svllm_lm_head_argmax_bf16(const void* hidden, int64_t num_rows, int64_t hidden_size,
+                              int64_t hidden_stride, const void* weight, int64_t vocab,
+                              int64_t weight_stride, int64_t* out_ids, void* logits,
+                              int64_t logits_stride, void* workspace, int64_t workspace_bytes,
+                              svllm_stream stream);
 
 /*
  * Reads (and with reset != 0 clears) the library's own error word on `device`. Synchronises

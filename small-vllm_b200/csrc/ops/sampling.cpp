@@ -45,6 +45,17 @@ at::Tensor greedy_sample(const at::Tensor& hidden, const at::Tensor& lm_head_wei
   TORCH_CHECK(hidden.scalar_type() == lm_head_weight.scalar_type() &&
                   hidden.device() == lm_head_weight.device(),
               "greedy_sample: hidden and lm_head_weight must share dtype and device");
+  if (hidden.is_cuda() && hidden.scalar_type() == at::kBFloat16 && hidden.numel() > 0 &&
+      hidden.stride(-1) == 1 && lm_head_weight.stride(1) == 1 &&
+      (hidden.dim() <= 2 || hidden.is_contiguous())) {
+    // the LM-head GEMM and the argmax in one pass, the logits never stored
+    const at::Tensor rows = hidden.dim() == 1 ? hidden.unsqueeze(0)
+                            : hidden.dim() == 2 ? hidden
+                                                : hidden.view({-1, hidden.size(-1)});
+    const std::vector<int64_t> shape(hidden.sizes().begin(), hidden.sizes().end() - 1);
+    at::Tensor out = at::empty(shape, hidden.options().dtype(at::kLong));
+    if (cuda_impl::lm_head_argmax(out.view({-1}), rows, lm_head_weight)) return out;
+  }
   return svllm::ops::argmax(at::matmul(hidden, lm_head_weight.t()));
 }
 

@@ -15,8 +15,12 @@ namespace svllm::ops {
 at::Tensor argmax(const at::Tensor& logits);
 
 // Definition: The model's last steps for greedy decoding with a tied (or any) LM head:
-//             logits = hidden @ lm_head_weight^T (a library GEMM: torch::matmul, cuBLAS on
-//             GPU), then argmax over the vocabulary. hidden is the final norm's output.
+//             logits = hidden @ lm_head_weight^T, then argmax over the vocabulary. hidden is
+//             the final norm's output. On CUDA (bf16) one fused tcgen05 kernel computes the
+//             GEMM in fp32, rounds each logit to bf16 as a bf16 matmul stores it and takes the
+//             argmax without storing the logits; it can differ from matmul-then-argmax only
+//             where a logit tied for the maximum rounds differently under the two GEMMs'
+//             accumulation orders. Elsewhere: torch::matmul, then argmax.
 // Domain:     hidden [..., H] and lm_head_weight [vocab, H] (the embedding table when
 //             tie_word_embeddings, src/model/config.h:28), same dtype and device.
 // Returns:    int64 token ids [...].

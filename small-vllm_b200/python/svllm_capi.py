@@ -64,6 +64,8 @@ SIGNATURES = {
     "svllm_embedding_f32": [_P, _P, _I, _P, _I64, _I64, _I64, _I64, _I64, _P, _P],
     "svllm_argmax_bf16": [_P, _I64, _I64, _I64, _P, _P],
     "svllm_argmax_f32": [_P, _I64, _I64, _I64, _P, _P],
+    "svllm_lm_head_argmax_bf16": [_P, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _I64,
+                                  _P],
     "svllm_read_device_error": [_I, _I, _P],
     "svllm_set_pipeline": [ctypes.c_char_p, _I64, _I64, _I64],
 }
@@ -227,6 +229,17 @@ def argmax(out_ids, logits, stream=None) -> None:
     fn = getattr(lib(), f"svllm_argmax_{_bf16_or_f32(logits)}")
     check(fn(logits.data_ptr(), rows, vocab, stride, out_ids.data_ptr(), _stream(stream)),
           "argmax")
+
+
+def lm_head_argmax(out_ids, hidden, weight, workspace, logits=None, stream=None) -> None:
+    """out_ids[r] = argmax_n bf16(hidden[r] . weight[n]); workspace: int64 [>= rows], zero."""
+    rows, hidden_size, hidden_stride = _rows(hidden)
+    vocab, _, weight_stride = _rows(weight)
+    check(lib().svllm_lm_head_argmax_bf16(
+        hidden.data_ptr(), rows, hidden_size, hidden_stride, weight.data_ptr(), vocab,
+        weight_stride, out_ids.data_ptr(), logits.data_ptr() if logits is not None else None,
+        logits.stride(0) if logits is not None else 0, workspace.data_ptr(),
+        workspace.numel() * workspace.element_size(), _stream(stream)), "lm_head_argmax")
 
 
 def read_device_error(device: int = 0, reset: bool = True) -> int:
