@@ -258,6 +258,22 @@ int svllm_lm_head_argmax_bf16(const void* hidden, int64_t num_rows, int64_t hidd
                               svllm_stream stream);
 
 /*
+ * svllm_lm_head_argmax_bf16 without a workspace argument, for callers that cannot allocate
+ * device memory: a host program driving this C ABI through an FFI with no CUDA allocator of its
+ * own, or one whose device memory is all owned by another allocator. It allocates nothing; the
+ * per-row scratch is an array inside this library (32 KB per GPU that loads it, held until the
+ * process exits), so num_rows is at most 4096 (SVLLM_ERR_TOO_LARGE beyond). The first call on a
+ * device looks the array's address up (make that call before any stream capture). Every call
+ * shares the array: each clears the rows it uses on its stream before the GEMM, and calls that
+ * overlap on the GPU (other streams, other host threads) race on it and must not.
+ * No counterpart in the reference: an addition of this library.
+ */
+int svllm_lm_head_argmax_static_bf16(const void* hidden, int64_t num_rows, int64_t hidden_size,
+                                     int64_t hidden_stride, const void* weight, int64_t vocab,
+                                     int64_t weight_stride, int64_t* out_ids, void* logits,
+                                     int64_t logits_stride, svllm_stream stream);
+
+/*
  * Reads (and with reset != 0 clears) the library's own error word on `device`. Synchronises
  * that device. For validation, not for the hot path.
  */

@@ -25,6 +25,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 #include <mutex>
 
@@ -680,4 +681,102 @@ extern "C" int svllm_lm_head_argmax_bf16(const void* hidden, int64_t num_rows,
   const int64_t blocks = (num_rows + 255) / 256;
   return launch(lm_head_argmax_finish_kernel, dim3(static_cast<unsigned>(blocks < 1024 ? blocks : 1024)),
                 dim3(256), 0, s, 1, a.keys, num_rows, out_ids);
+}
+
+// ---------------------------------------------------------------------------------------------
+// The same LM head and greedy sampling without a caller workspace: the per-row keys live in a
+// file-scope array of this library. It serves callers that cannot allocate device memory, such
+// as a host program driving this C ABI through an FFI (ctypes, cgo, JNI) that has no CUDA
+// allocator of its own, or one whose device memory is entirely owned by another allocator.
+
+namespace svllm::k {
+
+// At most this many rows per call: 4096 keys of 8 bytes, 32 KB that every GPU which loads the
+// library holds until the process exits.
+constexpr int64_t kStaticScratchRows = 4096;
+
+// The keys of svllm_lm_head_argmax_static_bf16. They must be zero when the GEMM starts; each
+// call clears the rows it uses first, and its last kernel clears them again.
+static __device__ __align__(256) uint64_t g_lm_head_static_keys[kStaticScratchRows];
+
+namespace {
+
+std::atomic<uint64_t*> g_static_keys_address[kMaxDevices];
+
+// The device address of g_lm_head_static_keys on `device` (the current device), looked up once
+// per device; null if the lookup fails.
+uint64_t* static_keys(int device) {
+  uint64_t* p = g_static_keys_address[device].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_lm_head_static_keys) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    p = static_cast<uint64_t*>(addr);
+    g_static_keys_address[device].store(p, std::memory_order_release);
+  }
+  return p;
+}
+
+}  // namespace
+}  // namespace svllm::k
+
+extern "C" int svllm_lm_head_argmax_static_bf16(const void* hidden, int64_t num_rows,
+                                                int64_t hidden_size, int64_t hidden_stride,
+                                                const void* weight, int64_t vocab,
+                                                int64_t weight_stride, int64_t* out_ids,
+                                                void* logits, int64_t logits_stride,
+                                                svllm_stream stream) {
+  using namespace svllm::k;
+  if (num_rows < 0 || hidden_size <= 0 || vocab <= 0 || hidden_stride < hidden_size ||
+      weight_stride < hidden_size || vocab >= (int64_t{1} << 31) ||
+      (logits != nullptr && logits_stride < vocab)) {
+    return SVLLM_ERR_INVALID_ARGUMENT;
+  }
+  if (num_rows > kStaticScratchRows) return SVLLM_ERR_TOO_LARGE;
+  if (num_rows == 0) return SVLLM_OK;
+  if (hidden == nullptr || weight == nullptr || out_ids == nullptr) {
+    return SVLLM_ERR_INVALID_ARGUMENT;
+  }
+  if (!aligned16(hidden) || !aligned16(weight) || (hidden_stride * 2) % 16 != 0 ||
+      (weight_stride * 2) % 16 != 0) {
+    return SVLLM_ERR_UNSUPPORTED;
+  }
+  int device;
+  if (current_device(&device) != SVLLM_OK) return SVLLM_ERR_CUDA;
+  int* err = library_error_word(device);
+  uint64_t* keys = static_keys(device);  // the first call on a device looks it up
+  if (err == nullptr || keys == nullptr) return SVLLM_ERR_CUDA;
+  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // the rows this call uses start at zero, whatever an earlier call left behind
+  if (cudaMemsetAsync(keys, 0, static_cast<size_t>(num_rows) * sizeof(uint64_t), s) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return SVLLM_ERR_CUDA;
+  }
+
+  LmHeadArgs a{};
+  a.m = num_rows;
+  a.n = vocab;
+  a.k = hidden_size;
+  a.keys = keys;
+  a.logits = logits;
+  a.logits_stride = logits_stride;
+  a.err = err;
+  int status;
+  if (num_rows <= kSwapMaxRows) {
+    status = launch_swap(hidden, hidden_stride, weight, weight_stride, a, device, s);
+  } else switch (pick_bn(num_rows, vocab, sm_count(device))) {
+    case 256: status = launch_gemm<256>(hidden, hidden_stride, weight, weight_stride, a, device, s); break;
+    case 224: status = launch_gemm<224>(hidden, hidden_stride, weight, weight_stride, a, device, s); break;
+    case 208: status = launch_gemm<208>(hidden, hidden_stride, weight, weight_stride, a, device, s); break;
+    case 192: status = launch_gemm<192>(hidden, hidden_stride, weight, weight_stride, a, device, s); break;
+    case 160: status = launch_gemm<160>(hidden, hidden_stride, weight, weight_stride, a, device, s); break;
+    default: status = launch_gemm<128>(hidden, hidden_stride, weight, weight_stride, a, device, s); break;
+  }
+  if (status != SVLLM_OK) return status;
+  const int64_t blocks = (num_rows + 255) / 256;
+  return launch(lm_head_argmax_finish_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s,
+                1, keys, num_rows, out_ids);
 }

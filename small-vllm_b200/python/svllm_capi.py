@@ -66,6 +66,7 @@ SIGNATURES = {
     "svllm_argmax_f32": [_P, _I64, _I64, _I64, _P, _P],
     "svllm_lm_head_argmax_bf16": [_P, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _I64,
                                   _P],
+    "svllm_lm_head_argmax_static_bf16": [_P, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P],
     "svllm_read_device_error": [_I, _I, _P],
     "svllm_set_pipeline": [ctypes.c_char_p, _I64, _I64, _I64],
 }
