@@ -258,6 +258,27 @@ int svllm_lm_head_argmax_bf16(const void* hidden, int64_t num_rows, int64_t hidd
                               svllm_stream stream);
 
 /*
+ * Decode attention over a paged KV cache (one query token per request): for request b and query
+ * head h, out[b, h] = softmax_j(scale * q[b, h] . k_j) v_j over the first seq_lens[b] cached
+ * rows of KV head h / (num_heads / num_kv_heads), row j at slot block_tables[b][j / block_size]
+ * * block_size + j % block_size of k_cache / v_cache [num_blocks, block_size, num_kv_heads,
+ * head_dim]. q: [num_seqs, num_heads, head_dim] at q_token_stride elements per request (a view
+ * of the qkv projection); out: [num_seqs, num_heads, head_dim] contiguous; block_tables:
+ * [num_seqs, max_blocks] int32; seq_lens: [num_seqs] int32, each at most max_seq_len (which
+ * sizes the context split). bf16, fp32 softmax and accumulation. head_dim 64 or 128, up to 8
+ * query heads per KV head (a power of two), 16-byte aligned q and caches, else
+ * SVLLM_ERR_UNSUPPORTED. A table entry outside the cache raises SVLLM_DEVERR_BAD_INDEX and reads
+ * block 0. New op: the reference plans this kernel (docs/ROADMAP.md, decode attention).
+ */
+int svllm_paged_decode_attention_bf16(void* out, const void* q, int64_t q_token_stride,
+                                      const void* k_cache, const void* v_cache,
+                                      int64_t num_blocks, int64_t block_size,
+                                      const int32_t* block_tables, int64_t max_blocks,
+                                      const int32_t* seq_lens, int64_t num_seqs,
+                                      int64_t num_heads, int64_t num_kv_heads, int64_t head_dim,
+                                      int64_t max_seq_len, float scale, svllm_stream stream);
+
+/*
  * svllm_lm_head_argmax_bf16 without a workspace argument, for callers that cannot allocate
  * device memory: a host program driving this C ABI through an FFI with no CUDA allocator of its
  * own, or one whose device memory is all owned by another allocator. It allocates nothing; the

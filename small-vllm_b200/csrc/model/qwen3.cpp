@@ -14,10 +14,13 @@
 #include "ops/sampling.h"
 #include "ops/silu_and_mul.h"
 
+#include "svllm_kernels.h"
+
 #ifdef SVLLM_CUDA
 #include <ATen/cuda/CUDAContext.h>
 #include <ATen/cuda/CUDAGraph.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
 #endif
 
 namespace svllm::model {
@@ -121,6 +124,42 @@ at::Tensor Model::attention(const at::Tensor& q, int64_t layer, const AttentionP
   return out.reshape({T, Hq * D});
 }
 
+bool Model::paged_decode_ok(const AttentionMetadata& meta) const {
+#ifdef SVLLM_CUDA
+  const int64_t group = config_.num_heads / config_.num_kv_heads;
+  return meta.decode && embed_.is_cuda() && embed_.scalar_type() == at::kBFloat16 &&
+         (config_.head_dim == 64 || config_.head_dim == 128) && group <= 8 &&
+         (group & (group - 1)) == 0;
+#else
+  (void)meta;
+  return false;
+#endif
+}
+
+at::Tensor Model::paged_decode_attention(const at::Tensor& q, int64_t layer,
+                                         const AttentionMetadata& meta) const {
+  const int64_t S = q.size(0), Hq = config_.num_heads, D = config_.head_dim;
+#ifdef SVLLM_CUDA
+  const at::Tensor tables = meta.block_tables.to(at::kInt).contiguous();
+  const at::Tensor lens = meta.seq_lens.to(at::kInt).contiguous();
+  at::Tensor out = at::empty({S, Hq, D}, q.options());
+  const c10::cuda::CUDAGuard device_guard(q.device());
+  const int status = svllm_paged_decode_attention_bf16(
+      out.data_ptr(), q.data_ptr(), q.stride(0), k_cache_[layer].data_ptr(),
+      v_cache_[layer].data_ptr(), num_blocks_, block_size_, tables.const_data_ptr<int32_t>(),
+      tables.size(1), lens.const_data_ptr<int32_t>(), S, Hq, config_.num_kv_heads, D,
+      tables.size(1) * block_size_, static_cast<float>(std::pow(static_cast<double>(D), -0.5)),
+      reinterpret_cast<svllm_stream>(c10::cuda::getCurrentCUDAStream().stream()));
+  TORCH_CHECK(status == SVLLM_OK, "Model: paged decode attention: ", svllm_status_string(status));
+  return out.view({S, Hq * D});
+#else
+  (void)layer;
+  (void)meta;
+  TORCH_CHECK(false, "Model: paged decode attention needs CUDA");
+  return at::Tensor();
+#endif
+}
+
 at::Tensor Model::forward(const at::Tensor& ids, const at::Tensor& positions,
                           const AttentionMetadata& meta) {
   TORCH_CHECK(!k_cache_.empty(), "Model::forward: allocate_kv_cache first");
@@ -138,7 +177,8 @@ at::Tensor Model::forward(const at::Tensor& ids, const at::Tensor& positions,
   const int64_t T = ids.size(0);
   const int64_t Hq = config_.num_heads, Hk = config_.num_kv_heads, D = config_.head_dim;
   const double eps = config_.rms_norm_eps;
-  const AttentionPlan plan = plan_attention(T, meta);
+  const bool paged = paged_decode_ok(meta);
+  const AttentionPlan plan = paged ? AttentionPlan{} : plan_attention(T, meta);
 
   at::Tensor hidden = ops::embedding(ids, embed_);
   at::Tensor residual;
@@ -162,7 +202,9 @@ at::Tensor Model::forward(const at::Tensor& ids, const at::Tensor& positions,
       ops::rope_cache(q, k, v, positions, meta.slot_mapping, k_cache_[l], v_cache_[l],
                       config_.rope_theta, config_.rope_scaling);
     }
-    hidden = at::linear(attention(q, static_cast<int64_t>(l), plan), layer.o_proj);
+    const at::Tensor attn = paged ? paged_decode_attention(q, static_cast<int64_t>(l), meta)
+                                  : attention(q, static_cast<int64_t>(l), plan);
+    hidden = at::linear(attn, layer.o_proj);
     ops::add_rms_norm(hidden, residual, layer.post_norm, eps);
     hidden = at::linear(ops::silu_and_mul(at::linear(hidden, layer.gate_up)), layer.down);
   }
@@ -181,7 +223,7 @@ at::Tensor Model::decode(const at::Tensor& ids, const at::Tensor& positions,
                          const at::Tensor& seq_lens) {
   const at::Tensor qsl = at::arange(
       ids.size(0) + 1, at::TensorOptions().dtype(at::kInt).device(ids.device()));
-  return greedy(forward(ids, positions, {slot_mapping, block_tables, seq_lens, qsl}));
+  return greedy(forward(ids, positions, {slot_mapping, block_tables, seq_lens, qsl, true}));
 }
 
 #ifdef SVLLM_CUDA

@@ -8,8 +8,9 @@
 // Per layer: add_rms_norm -> one qkv GEMM -> qk_norm_rope_cache (Qwen3) or rope_cache (Llama),
 // which also writes k and v into the paged cache -> attention over the cache -> o GEMM ->
 // add_rms_norm -> one gate_up GEMM -> silu_and_mul -> down GEMM. GEMMs are torch::linear
-// (cuBLAS on GPU, as the reference plans, docs/ROADMAP.md:16); attention is a LibTorch composite
-// over the gathered cache (the reference's own attention kernels are not built yet).
+// (cuBLAS on GPU, as the reference plans, docs/ROADMAP.md:16). Attention: on CUDA decode steps
+// the paged decode-attention kernel reads the cache in place; otherwise (prefill, mixed steps,
+// CPU) a LibTorch composite over the gathered cache.
 
 #include <ATen/ATen.h>
 
@@ -37,6 +38,7 @@ struct AttentionMetadata {
   at::Tensor block_tables;
   at::Tensor seq_lens;
   at::Tensor query_start_loc;
+  bool decode = false;  // every request has one query token (query_start_loc = 0..S)
 };
 
 // A decoder-only Qwen3 or Llama model. Weights are taken by their Hugging Face names; q/k/v and
@@ -92,6 +94,10 @@ class Model {
   };
   AttentionPlan plan_attention(int64_t tokens, const AttentionMetadata& meta) const;
   at::Tensor attention(const at::Tensor& q, int64_t layer, const AttentionPlan& plan) const;
+  // Decode steps on CUDA: the paged decode-attention kernel straight from the cache.
+  bool paged_decode_ok(const AttentionMetadata& meta) const;
+  at::Tensor paged_decode_attention(const at::Tensor& q, int64_t layer,
+                                    const AttentionMetadata& meta) const;
 
   ModelConfig config_;
   at::Tensor embed_;       // [V, H]

@@ -67,6 +67,8 @@ SIGNATURES = {
     "svllm_lm_head_argmax_bf16": [_P, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _I64,
                                   _P],
     "svllm_lm_head_argmax_static_bf16": [_P, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P],
+    "svllm_paged_decode_attention_bf16": [_P, _P, _I64, _P, _P, _I64, _I64, _P, _I64, _P, _I64,
+                                          _I64, _I64, _I64, _I64, ctypes.c_float, _P],
     "svllm_read_device_error": [_I, _I, _P],
     "svllm_set_pipeline": [ctypes.c_char_p, _I64, _I64, _I64],
 }
@@ -241,6 +243,18 @@ def lm_head_argmax(out_ids, hidden, weight, workspace, logits=None, stream=None)
         weight_stride, out_ids.data_ptr(), logits.data_ptr() if logits is not None else None,
         logits.stride(0) if logits is not None else 0, workspace.data_ptr(),
         workspace.numel() * workspace.element_size(), _stream(stream)), "lm_head_argmax")
+
+
+def paged_decode_attention(out, q, k_cache, v_cache, block_tables, seq_lens, max_seq_len: int,
+                           scale: float, stream=None) -> None:
+    """out [S, Hq, D] = decode attention of q [S, Hq, D] over the paged caches."""
+    num_seqs, num_heads, head_dim = q.shape
+    num_blocks, block_size, num_kv_heads, _ = k_cache.shape
+    check(lib().svllm_paged_decode_attention_bf16(
+        out.data_ptr(), q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+        num_blocks, block_size, block_tables.data_ptr(), block_tables.shape[1],
+        seq_lens.data_ptr(), num_seqs, num_heads, num_kv_heads, head_dim, max_seq_len, scale,
+        _stream(stream)), "paged_decode_attention")
 
 
 def read_device_error(device: int = 0, reset: bool = True) -> int:

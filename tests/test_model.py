@@ -142,6 +142,9 @@ def test_mixed_step_prefill_and_decode(device):
 
 
 def test_decode_entry_point_equals_forward_then_greedy(device):
+    """decode() is forward() + greedy() for one-token steps. On CUDA its attention is the paged
+    decode kernel instead of the gather + SDPA composite, so the ids must agree wherever the
+    composite's top two logits differ by more than the bar."""
     _, model = tiny("qwen3", device)
     g = torch.Generator().manual_seed(13)
     prompts = [torch.randint(0, VOCAB, (n,), generator=g) for n in (9, 17)]
@@ -150,8 +153,13 @@ def test_decode_entry_point_equals_forward_then_greedy(device):
     inputs = reqs.step_inputs([torch.tensor([3]), torch.tensor([4])])
     qsl = inputs.pop("query_start_loc")
     assert qsl.tolist() == [0, 1, 2]
-    want = model.greedy(model.forward(query_start_loc=qsl, **inputs))
-    assert torch.equal(model.decode(**inputs), want)
+    logits = model.logits(model.forward(query_start_loc=qsl, **inputs)).float()
+    got = model.decode(**inputs)
+    if device.type == "cpu":
+        assert torch.equal(got, model.greedy(model.forward(query_start_loc=qsl, **inputs)))
+    top2 = logits.topk(2, dim=-1).values
+    clear = (top2[:, 0] - top2[:, 1]) > REL_BAR * logits.abs().max()
+    assert torch.equal(got[clear], logits.argmax(-1)[clear])
 
 
 def test_padding_slot_writes_nothing(device):
