@@ -9,11 +9,12 @@
 // steps, the gather-then-SDPA composite of the model forward; the reference plans the kernel
 // ("Decode attention: Split-KV paged kernel, GQA-aware", docs/ROADMAP.md).
 //
-// A CTA of 128 threads owns (request, KV head, context split). It walks its share of the
-// context in sub-chunks of kSub tokens: scores into shared memory (D/8 lanes per row, one
-// 16-byte load each), an online-softmax rescale, then p * v accumulated per lane over 8
-// consecutive dims. Splits of one (request, KV head) form a thread-block cluster whose CTAs
-// merge their (max, sum, partial output) through distributed shared memory, each writing a
+// A CTA of 128 threads owns (request, KV head, context split), and each of its 4 warps a
+// contiguous share of that split. A warp streams its rows kUnroll per lane at a time, the K and
+// V loads (16 bytes each, D/8 lanes per row) in flight together, and keeps its own online
+// softmax (running max and sum by shuffles) and p * v accumulators: no block barrier until the
+// warps merge at the end. Splits of one (request, KV head) form a thread-block cluster whose
+// CTAs merge their (max, sum, partial output) through distributed shared memory, each writing a
 // slice of the bf16 output. Scores, softmax and accumulation are fp32. No scratch memory, one
 // launch.
 #include <cuda_runtime.h>
@@ -27,9 +28,8 @@ namespace svllm::k {
 namespace {
 
 constexpr int kThreads = 128;
-constexpr int kSub = 256;       // context tokens per sub-chunk
 constexpr int kMaxSplits = 8;   // the portable cluster size
-constexpr int kUnroll = 8;      // cache rows a lane has in flight
+constexpr int kMaxUnroll = 8;   // cache rows a lane has in flight (fewer when more CTAs must fit)
 
 struct AttnArgs {
   void* out;                 // [num_seqs, num_heads, head_dim] bf16, contiguous
@@ -70,62 +70,41 @@ __device__ __forceinline__ float ld_remote_f32(const float* p, uint32_t rank) {
   return v;
 }
 
-// Block-wide reduction of G floats per thread (max or sum) into `red` [warps][G]; every thread
-// gets the G results. One barrier; `red` must not be rewritten before the next barrier.
-template <bool kMax, int G>
-__device__ __forceinline__ void block_reduce(float (&v)[G], float (*red)[G]) {
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-#pragma unroll
-    for (int off = 16; off > 0; off /= 2) {
-      const float o = __shfl_xor_sync(0xffffffffu, v[g], off);
-      v[g] = kMax ? fmaxf(v[g], o) : v[g] + o;
-    }
-  }
-  const int warp = threadIdx.x / kWarpSize;
-  if (threadIdx.x % kWarpSize == 0) {
-#pragma unroll
-    for (int g = 0; g < G; ++g) red[warp][g] = v[g];
-  }
-  __syncthreads();
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float r = red[0][g];
-#pragma unroll
-    for (int w = 1; w < kThreads / kWarpSize; ++w) r = kMax ? fmaxf(r, red[w][g]) : r + red[w][g];
-    v[g] = r;
-  }
-}
-
-template <int D, int G>
+template <int D, int G, int kUnroll>
 __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnArgs a) {
   grid_dependency_sync();
-  constexpr int kLpr = D / 8;              // lanes per cache row, 8 dims (16 bytes) each
-  constexpr int kRows = kThreads / kLpr;   // rows in flight per pass
+  constexpr int kLpr = D / 8;                  // lanes per cache row, 8 dims (16 bytes) each
+  constexpr int kGroups = kWarpSize / kLpr;    // rows one warp-wide load covers
+  constexpr int kStep = kGroups * kUnroll;     // rows per warp per iteration
+  constexpr int kWarps = kThreads / kWarpSize;
   static_assert(kWarpSize % kLpr == 0, "a row's lanes stay in one warp");
 
-  __shared__ float scores[G][kSub];
-  __shared__ float red_max[kThreads / kWarpSize][G];
-  __shared__ float red_sum[kThreads / kWarpSize][G];
-  __shared__ float part[kRows][G][D];  // per row group: partial outputs, summed at the end
+  __shared__ float warp_m[kWarps][G], warp_l[kWarps][G];
+  __shared__ float warp_acc[kWarps][G][D];
   __shared__ float m_sm[G], l_sm[G];
-  __shared__ int64_t slot_base[kSub + 1];  // the sub-chunk's blocks, first slot of each
+  __shared__ float part[G][D];
 
   const int split = static_cast<int>(blockIdx.x % a.splits);
   const int64_t pair = blockIdx.x / a.splits;
   const int64_t b = pair / a.num_kv_heads;
   const int kh = static_cast<int>(pair % a.num_kv_heads);
-  const int rg = threadIdx.x / kLpr;   // row group
-  const int sub = threadIdx.x % kLpr;  // this lane's 8 dims: [8 sub, 8 sub + 8)
+  const int warp = threadIdx.x / kWarpSize;
+  const int lane = threadIdx.x % kWarpSize;
+  const int grp = lane / kLpr;  // which of the warp's kGroups rows this lane reads
+  const int sub = lane % kLpr;  // this lane's 8 dims: [8 sub, 8 sub + 8)
 
   int seq_len = a.seq_lens[b];
   if (seq_len < 0 || seq_len > a.max_blocks * a.block_size) {  // past the block table
     if (threadIdx.x == 0) raise_error(a.err, kErrBadIndex);
     seq_len = seq_len < 0 ? 0 : a.max_blocks * a.block_size;
   }
+  // this CTA's split of the context, then this warp's contiguous share of it
   const int chunk = (seq_len + a.splits - 1) / a.splits;
-  const int j_begin = min(seq_len, split * chunk);
-  const int j_end = min(seq_len, j_begin + chunk);
+  const int c_begin = min(seq_len, split * chunk);
+  const int c_end = min(seq_len, c_begin + chunk);
+  const int per_warp = (c_end - c_begin + kWarps - 1) / kWarps;
+  const int w_begin = min(c_end, c_begin + warp * per_warp);
+  const int w_end = min(c_end, w_begin + per_warp);
   const int32_t* table = a.block_tables + b * a.max_blocks;
 
   // this lane's slice of each query head, fp32
@@ -154,127 +133,140 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnAr
   const Bf16::Storage* kc = static_cast<const Bf16::Storage*>(a.k_cache);
   const Bf16::Storage* vc = static_cast<const Bf16::Storage*>(a.v_cache);
 
-  for (int s0 = j_begin; s0 < j_end; s0 += kSub) {
-    const int n = min(kSub, j_end - s0);
-    // the sub-chunk's block-table entries, once, as first slots
-    const int blk0 = s0 / a.block_size;
-    const int nblk = (s0 + n - 1) / a.block_size - blk0 + 1;
-    for (int t = threadIdx.x; t < nblk; t += kThreads) {
-      int blk = table[blk0 + t];
-      if (blk < 0 || blk >= a.num_blocks) {  // an entry outside the cache: read block 0
-        raise_error(a.err, kErrBadIndex);
-        blk = 0;
-      }
-      slot_base[t] = static_cast<int64_t>(blk) * a.block_size;
-    }
-    __syncthreads();
-    auto row_offset = [&](int i) -> int64_t {  // element offset of sub-chunk row i, this head
-      const int j = s0 + i;
-      return (slot_base[j / a.block_size - blk0] + j % a.block_size) * row_elems + head_offset;
-    };
-    // scores of this sub-chunk, kUnroll rows per lane in flight; the loop is warp-uniform
-    // (a row's lanes reduce by shuffles)
-    for (int i0 = 0; i0 < n; i0 += kRows * kUnroll) {
-      uint4 raw[kUnroll];
+  // Each iteration: kUnroll rows per lane, K and V loads all in flight together; the scores of
+  // the warp's kStep rows, their running max and sum by shuffles, then p * v into this lane's 8
+  // dims. No block-wide barrier until the warps meet at the end.
+  for (int r0 = w_begin; r0 < w_end; r0 += kStep) {
+    uint4 kraw[kUnroll], vraw[kUnroll];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int i = i0 + u * kRows + rg;
-        raw[u] = i < n ? ld_global_nc_v4(kc + row_offset(i)) : make_uint4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int i = i0 + u * kRows + rg;
-        float kf[8];
-        unpack<Bf16>(raw[u], kf);
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          float d = 0.0f;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) d = __fmaf_rn(q[g][e], kf[e], d);
-#pragma unroll
-          for (int off = kLpr / 2; off > 0; off /= 2) d += __shfl_xor_sync(0xffffffffu, d, off);
-          if (sub == 0 && i < n) scores[g][i] = d * a.scale;
+    for (int u = 0; u < kUnroll; ++u) {
+      const int j = r0 + u * kGroups + grp;
+      if (j < w_end) {
+        int blk = __ldg(table + j / a.block_size);
+        if (blk < 0 || blk >= a.num_blocks) {  // an entry outside the cache: read block 0
+          raise_error(a.err, kErrBadIndex);
+          blk = 0;
         }
+        const int64_t off = (static_cast<int64_t>(blk) * a.block_size + j % a.block_size) *
+                                row_elems + head_offset;
+        kraw[u] = ld_global_nc_v4(kc + off);
+        vraw[u] = ld_global_nc_v4(vc + off);
+      } else {
+        kraw[u] = make_uint4(0, 0, 0, 0);
+        vraw[u] = make_uint4(0, 0, 0, 0);
       }
     }
-    __syncthreads();
-    // online softmax: new running max, rescale what is accumulated, p = exp(s - max)
-    float cm[G];
+    float s[kUnroll][G];
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      cm[g] = -__builtin_huge_valf();
-      for (int i = threadIdx.x; i < n; i += kThreads) cm[g] = fmaxf(cm[g], scores[g][i]);
+    for (int u = 0; u < kUnroll; ++u) {
+      const bool valid = r0 + u * kGroups + grp < w_end;
+      float kf[8];
+      unpack<Bf16>(kraw[u], kf);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float d = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) d = __fmaf_rn(q[g][e], kf[e], d);
+#pragma unroll
+        for (int off = kLpr / 2; off > 0; off /= 2) d += __shfl_xor_sync(0xffffffffu, d, off);
+        s[u][g] = valid ? d * a.scale : -__builtin_huge_valf();
+      }
     }
-    block_reduce<true>(cm, red_max);
-    float ps[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const float m_new = fmaxf(m[g], cm[g]);
+      float mx = s[0][g];
+#pragma unroll
+      for (int u = 1; u < kUnroll; ++u) mx = fmaxf(mx, s[u][g]);
+#pragma unroll
+      for (int off = kLpr; off < kWarpSize; off *= 2) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      }
+      const float m_new = fmaxf(m[g], mx);  // finite: the iteration has a valid row
       const float alpha = __expf(m[g] - m_new);
-      ps[g] = 0.0f;
-      for (int i = threadIdx.x; i < n; i += kThreads) {
-        const float p = __expf(scores[g][i] - m_new);
-        scores[g][i] = p;
-        ps[g] += p;
+      float ps = 0.0f;
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        s[u][g] = __expf(s[u][g] - m_new);  // 0 for rows past the share
+        ps += s[u][g];
       }
-      l[g] *= alpha;
+#pragma unroll
+      for (int off = kLpr; off < kWarpSize; off *= 2) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+      l[g] = l[g] * alpha + ps;
       m[g] = m_new;
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[g][e] *= alpha;
     }
-    block_reduce<false>(ps, red_sum);  // its barrier also publishes the p values
 #pragma unroll
-    for (int g = 0; g < G; ++g) l[g] += ps[g];
-    // p * v over this lane's 8 dims, kUnroll rows in flight
-    for (int i0 = 0; i0 < n; i0 += kRows * kUnroll) {
-      uint4 raw[kUnroll];
+    for (int u = 0; u < kUnroll; ++u) {
+      float vf[8];
+      unpack<Bf16>(vraw[u], vf);
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int i = i0 + u * kRows + rg;
-        raw[u] = i < n ? ld_global_nc_v4(vc + row_offset(i)) : make_uint4(0, 0, 0, 0);
-      }
+      for (int g = 0; g < G; ++g) {
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int i = i0 + u * kRows + rg;
-        if (i < n) {
-          float vf[8];
-          unpack<Bf16>(raw[u], vf);
-#pragma unroll
-          for (int g = 0; g < G; ++g) {
-            const float p = scores[g][i];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[g][e] = __fmaf_rn(p, vf[e], acc[g][e]);
-          }
-        }
+        for (int e = 0; e < 8; ++e) acc[g][e] = __fmaf_rn(s[u][g], vf[e], acc[g][e]);
       }
     }
-    __syncthreads();  // scores and slot_base are rewritten by the next sub-chunk
   }
-
-  // the row groups' partial outputs summed: part[0] holds this CTA's result
+  // the warp's row groups hold partial sums of the same dims: add them up
 #pragma unroll
   for (int g = 0; g < G; ++g) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) part[rg][g][sub * 8 + e] = acc[g][e];
+    for (int e = 0; e < 8; ++e) {
+#pragma unroll
+      for (int off = kLpr; off < kWarpSize; off *= 2) {
+        acc[g][e] += __shfl_xor_sync(0xffffffffu, acc[g][e], off);
+      }
+    }
   }
-  if (threadIdx.x < G) {
-    m_sm[threadIdx.x] = m[threadIdx.x];
-    l_sm[threadIdx.x] = l[threadIdx.x];
+  if (grp == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) warp_acc[warp][g][sub * 8 + e] = acc[g][e];
+    }
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      warp_m[warp][g] = m[g];
+      warp_l[warp][g] = l[g];
+    }
   }
   __syncthreads();
+  // the warps' (max, sum, partial) merged into the CTA's
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
+    float mx = warp_m[0][g];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, warp_m[w][g]);
+    float ls = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      ls += warp_m[w][g] == -__builtin_huge_valf() ? 0.0f : warp_l[w][g] * __expf(warp_m[w][g] - mx);
+    }
+    m_sm[g] = mx;
+    l_sm[g] = ls;
+  }
   for (int idx = threadIdx.x; idx < G * D; idx += kThreads) {
     const int g = idx / D, d = idx % D;
-    float s = part[0][g][d];
-    for (int r = 1; r < kRows; ++r) s += part[r][g][d];
-    part[0][g][d] = s;
+    float mx = warp_m[0][g];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, warp_m[w][g]);
+    float o = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      o += warp_m[w][g] == -__builtin_huge_valf() ? 0.0f
+                                                    : warp_acc[w][g][d] * __expf(warp_m[w][g] - mx);
+    }
+    part[g][d] = o;
   }
+  __syncthreads();
 
   __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (b * a.num_kv_heads + kh) * G * D;
   if (a.splits == 1) {
-    __syncthreads();
     for (int idx = threadIdx.x; idx < G * D; idx += kThreads) {
       const int g = idx / D;
-      out[idx] = __float2bfloat16_rn(l_sm[g] > 0.0f ? part[0][g][idx % D] / l_sm[g] : 0.0f);
+      out[idx] = __float2bfloat16_rn(l_sm[g] > 0.0f ? part[g][idx % D] / l_sm[g] : 0.0f);
     }
     return;
   }
@@ -291,7 +283,7 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnAr
       if (r < a.splits) {
         mr[r] = ld_remote_f32(&m_sm[g], r);
         lr[r] = ld_remote_f32(&l_sm[g], r);
-        pr[r] = ld_remote_f32(&part[0][g][d], r);
+        pr[r] = ld_remote_f32(&part[g][d], r);
       }
     }
     float mx = -__builtin_huge_valf();
@@ -313,21 +305,33 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnAr
   cluster_sync_all();  // every CTA's shared memory stays valid until the others have read it
 }
 
+// Rows in flight per lane: 8 while every CTA of the launch is resident at once (each warp's
+// latency chain is then what bounds it), 4 when the CTAs run in waves (then occupancy does);
+// half of that with 8 query heads per KV head, whose accumulators take the registers. Measured
+// on a B200: 64 requests x 512 tokens 36 us at 8 rows, 44 us at 4; 256 requests 141 vs 128 us.
 template <int D, int G>
-int launch_attention(const AttnArgs& a, int64_t num_seqs, cudaStream_t stream) {
+int launch_attention(const AttnArgs& a, int64_t num_seqs, int device, cudaStream_t stream) {
+  constexpr int kDeep = G >= 8 ? kMaxUnroll / 2 : kMaxUnroll;
   const int64_t blocks = num_seqs * a.num_kv_heads * a.splits;
-  return launch(decode_attention_kernel<D, G>, dim3(static_cast<unsigned>(blocks)),
-                dim3(kThreads), 0, stream, a.splits > 1 ? static_cast<unsigned>(a.splits) : 1u,
-                a);
+  const unsigned cluster = a.splits > 1 ? static_cast<unsigned>(a.splits) : 1u;
+  const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(decode_attention_kernel<D, G, kDeep>),
+                                   kThreads, 0, device);
+  if (blocks <= static_cast<int64_t>(sm_count(device)) * (per_sm > 0 ? per_sm : 1)) {
+    return launch(decode_attention_kernel<D, G, kDeep>, dim3(static_cast<unsigned>(blocks)),
+                  dim3(kThreads), 0, stream, cluster, a);
+  }
+  return launch(decode_attention_kernel<D, G, kDeep / 2>, dim3(static_cast<unsigned>(blocks)),
+                dim3(kThreads), 0, stream, cluster, a);
 }
 
 template <int D>
-int dispatch_group(const AttnArgs& a, int64_t num_seqs, int group, cudaStream_t stream) {
+int dispatch_group(const AttnArgs& a, int64_t num_seqs, int group, int device,
+                   cudaStream_t stream) {
   switch (group) {
-    case 1: return launch_attention<D, 1>(a, num_seqs, stream);
-    case 2: return launch_attention<D, 2>(a, num_seqs, stream);
-    case 4: return launch_attention<D, 4>(a, num_seqs, stream);
-    case 8: return launch_attention<D, 8>(a, num_seqs, stream);
+    case 1: return launch_attention<D, 1>(a, num_seqs, device, stream);
+    case 2: return launch_attention<D, 2>(a, num_seqs, device, stream);
+    case 4: return launch_attention<D, 4>(a, num_seqs, device, stream);
+    case 8: return launch_attention<D, 8>(a, num_seqs, device, stream);
     default: return SVLLM_ERR_UNSUPPORTED;
   }
 }
@@ -386,6 +390,6 @@ extern "C" int svllm_paged_decode_attention_bf16(
   while (pow2 * 2 <= splits && pow2 * 2 <= kMaxSplits) pow2 *= 2;
   a.splits = pow2;
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return head_dim == 128 ? dispatch_group<128>(a, num_seqs, static_cast<int>(group), s)
-                         : dispatch_group<64>(a, num_seqs, static_cast<int>(group), s);
+  return head_dim == 128 ? dispatch_group<128>(a, num_seqs, static_cast<int>(group), device, s)
+                         : dispatch_group<64>(a, num_seqs, static_cast<int>(group), device, s);
 }

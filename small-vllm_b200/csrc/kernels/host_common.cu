@@ -4,6 +4,7 @@
 #include <atomic>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 
 #include "host_common.h"
 
@@ -36,25 +37,30 @@ PipelineShape g_shapes[static_cast<int>(OpId::kCount)] = {
 const char* const kOpNames[] = {"rms_norm", "add_rms_norm", "qk_norm_rope",
                                 "rope",     "silu_and_mul", "embedding"};
 
-struct OccEntry {
+// Occupancy per (kernel, block size, dynamic shared memory, device), and the kernels whose
+// shared-memory limit is raised on each device: looked up on every launch, so hashed.
+struct OccKey {
   const void* func;
   int threads;
   size_t smem;
   int device;
-  int blocks;
+  bool operator==(const OccKey& o) const {
+    return func == o.func && threads == o.threads && smem == o.smem && device == o.device;
+  }
+};
+
+struct OccKeyHash {
+  size_t operator()(const OccKey& k) const {
+    size_t h = std::hash<const void*>()(k.func);
+    h = h * 1000003u ^ std::hash<int>()(k.threads);
+    h = h * 1000003u ^ std::hash<size_t>()(k.smem);
+    return h * 1000003u ^ std::hash<int>()(k.device);
+  }
 };
 
 std::mutex g_occ_mutex;
-constexpr int kOccCacheSize = 256;
-OccEntry g_occ[kOccCacheSize];
-int g_occ_used = 0;
-
-struct AttrEntry {
-  const void* func;
-  int device;
-};
-AttrEntry g_attr[kOccCacheSize];
-int g_attr_used = 0;
+std::unordered_map<OccKey, int, OccKeyHash> g_occ;
+std::unordered_map<OccKey, bool, OccKeyHash> g_attr;  // keyed by (func, device) only
 
 }  // namespace
 
@@ -96,20 +102,11 @@ int sm_count(int device) {
 
 int blocks_per_sm(const void* func, int threads, size_t smem_bytes, int device) {
   const std::lock_guard<std::mutex> lock(g_occ_mutex);
-  for (int i = 0; i < g_occ_used; ++i) {
-    const OccEntry& e = g_occ[i];
-    if (e.func == func && e.threads == threads && e.smem == smem_bytes && e.device == device) {
-      return e.blocks;
-    }
-  }
-  bool attr_set = false;
-  for (int i = 0; i < g_attr_used; ++i) {
-    if (g_attr[i].func == func && g_attr[i].device == device) {
-      attr_set = true;
-      break;
-    }
-  }
-  if (!attr_set) {
+  const OccKey key{func, threads, smem_bytes, device};
+  const auto hit = g_occ.find(key);
+  if (hit != g_occ.end()) return hit->second;
+  const OccKey attr_key{func, 0, 0, device};
+  if (g_attr.find(attr_key) == g_attr.end()) {
     // the dynamic limit is what the CTA's static shared memory leaves of the per-CTA maximum
     cudaFuncAttributes attrs{};
     if (cudaFuncGetAttributes(&attrs, func) != cudaSuccess) {
@@ -124,7 +121,7 @@ int blocks_per_sm(const void* func, int threads, size_t smem_bytes, int device) 
       cudaGetLastError();
       return 0;
     }
-    if (g_attr_used < kOccCacheSize) g_attr[g_attr_used++] = {func, device};
+    g_attr.emplace(attr_key, true);
   }
   int blocks = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, func, threads, smem_bytes) !=
@@ -132,7 +129,7 @@ int blocks_per_sm(const void* func, int threads, size_t smem_bytes, int device) 
     cudaGetLastError();
     return 0;
   }
-  if (g_occ_used < kOccCacheSize) g_occ[g_occ_used++] = {func, threads, smem_bytes, device, blocks};
+  g_occ.emplace(key, blocks);
   return blocks;
 }
 
