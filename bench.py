@@ -88,16 +88,19 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload",
-                   choices=sorted(WORKLOADS) + ["sampling", "lm-head", "model-decode"],
+                   choices=sorted(WORKLOADS) + ["sampling", "lm-head", "model-decode",
+                                                "decode-attention"],
                    default="sweep",
                    help="sampling: greedy argmax over [tokens, 151936] bf16 logits (one op, "
                         "not the chain); lm-head: the tied LM head fused with greedy sampling "
                         "(one tcgen05 kernel) beside matmul + argmax; model-decode: Qwen3-0.6B "
-                        "decode steps through the model forward, eager and from CUDA graphs")
+                        "decode steps through the model forward, eager and from CUDA graphs; "
+                        "decode-attention: the paged decode-attention kernel of one Qwen3-0.6B "
+                        "layer beside the gather + SDPA composite it replaces")
     p.add_argument("--batches", default="1,8,64,256",
                    help="model-decode: comma-separated decode batch sizes")
     p.add_argument("--context", type=int, default=512,
-                   help="model-decode: KV-cache tokens per request")
+                   help="model-decode, decode-attention: KV-cache tokens per request")
     p.add_argument("--tokens", type=int, default=0, help="override total tokens")
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -622,6 +625,95 @@ def run_model_decode(args) -> int:
     return 0
 
 
+def run_decode_attention(args) -> int:
+    """Paged decode attention of one Qwen3-0.6B layer (16 query heads over 8 KV heads of 128,
+    block size 16) at each `--batches` size with `--context` cached tokens per request, through
+    the C ABI (svllm_paged_decode_attention_bf16), beside the composite it replaces in the model
+    forward: gather each request's K/V pages, then torch SDPA. The block tables are a random
+    permutation of the cache's blocks, so the pages a request reads are scattered."""
+    import torch
+    import torch.nn.functional as F
+
+    import svllm_capi as capi
+
+    cfg, block = QWEN3, 16
+    hq, hk, d = cfg["heads"], cfg["kv_heads"], cfg["head_dim"]
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    peaks = measured_peaks()
+    scale = d ** -0.5
+
+    def replay_us(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(args.steps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        graph.replay()
+        stop.record()
+        torch.cuda.synchronize()
+        return start.elapsed_time(stop) / args.steps * 1e3
+
+    for b in [int(x) for x in args.batches.split(",")]:
+        per_seq = -(-args.context // block)
+        blocks = b * per_seq
+        k_cache = torch.randn(blocks, block, hk, d, device=dev, generator=g).to(torch.bfloat16)
+        v_cache = torch.randn(blocks, block, hk, d, device=dev, generator=g).to(torch.bfloat16)
+        tables = torch.randperm(blocks, device=dev, generator=g).view(b, per_seq).int()
+        seq_lens = torch.full((b,), args.context, device=dev, dtype=torch.int32)
+        q = torch.randn(b, hq, d, device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty_like(q)
+        max_len = per_seq * block
+
+        def kernel():
+            capi.paged_decode_attention(out, q, k_cache, v_cache, tables, seq_lens, max_len,
+                                        scale)
+
+        slots = (tables.long()[:, :, None] * block
+                 + torch.arange(block, device=dev)).view(b, -1)[:, :args.context]
+
+        def composite():
+            k = k_cache.view(-1, hk, d).index_select(0, slots.reshape(-1)).view(b, -1, hk, d)
+            v = v_cache.view(-1, hk, d).index_select(0, slots.reshape(-1)).view(b, -1, hk, d)
+            return F.scaled_dot_product_attention(q[:, :, None], k.transpose(1, 2),
+                                                  v.transpose(1, 2), scale=scale,
+                                                  enable_gqa=True)[:, :, 0]
+
+        us = replay_us(kernel)
+        ref_us = replay_us(composite)
+        kernel()
+        ref = composite().float()
+        err = float((out.float() - ref).abs().max())
+        # algorithmic bytes: the K and V rows each request reads, q, out, its table row and length
+        traffic = (2 * b * args.context * hk * d * 2 + 2 * b * hq * d * 2 + b * per_seq * 4
+                   + b * 4)
+        gbs = traffic / (us * 1e-6) / 1e9
+        print(json.dumps({
+            "metric": "paged decode attention (KV bytes streamed per second)",
+            "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(us / 1e3, 5), "us_per_launch": round(us, 2),
+            "higher_is_better": True, "dtype": "bf16 (fp32 softmax and accumulation)",
+            "data": "synthetic (random q and KV cache, scattered pages)",
+            "config": {"workload": "Qwen3-0.6B layer decode attention", "batch": b,
+                       "context": args.context, "heads": hq, "kv_heads": hk, "head_dim": d,
+                       "block_size": block, "kv_bytes": 2 * b * args.context * hk * d * 2,
+                       "timing": "CUDA graph replay of the steps"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1),
+                         "peak": float(peaks["hbm_gbs"]),
+                         "unit": "GB/s", "frac": round(gbs / float(peaks["hbm_gbs"]), 4)},
+            "gather_then_sdpa_us": round(ref_us, 2), "speedup": round(ref_us / us, 3),
+            "max_abs_err_vs_sdpa": round(err, 6),
+            "gpu_launches": args.steps}), flush=True)
+        del k_cache, v_cache
+    return 0
+
+
 def main() -> int:
     args = parse_args()
     if args.workload == "sampling":
@@ -630,6 +722,8 @@ def main() -> int:
         return run_model_decode(args)
     if args.workload == "lm-head":
         return run_lm_head(args)
+    if args.workload == "decode-attention":
+        return run_decode_attention(args)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)
