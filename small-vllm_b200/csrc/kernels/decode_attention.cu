@@ -10,15 +10,18 @@
 // ("Decode attention: Split-KV paged kernel, GQA-aware", docs/ROADMAP.md).
 //
 // A CTA of 128 threads owns (request, KV head, context split), and each of its 4 warps a
-// contiguous share of that split. A warp streams its rows kUnroll per lane at a time, the K and
-// V loads (16 bytes each, D/8 lanes per row) in flight together, and keeps its own online
-// softmax (running max and sum by shuffles) and p * v accumulators: no block barrier until the
-// warps merge at the end. Splits of one (request, KV head) form a thread-block cluster whose
-// CTAs merge their (max, sum, partial output) through distributed shared memory, each writing a
-// slice of the bf16 output. Scores, softmax and accumulation are fp32. No scratch memory, one
-// launch.
+// contiguous share of that split, in tiles of 16 cache rows. Both products of a tile run on the
+// tensor cores (mma.sync m16n8k16, bf16 in, fp32 accumulate), with the query heads of the KV
+// head as the N = 8 columns: S^T = K Q^T straight from the rows a lane loads, then P^T (the
+// tile's softmax numerators, rounded to bf16 as flash attention does) and V^T transposed in
+// registers by movmatrix for O^T += V^T P^T. The running max and sum are per warp (base-2
+// exponent domain); the accumulators are rescaled only when the max moves. Splits of one
+// (request, KV head) form a thread-block cluster whose CTAs merge their (max, sum, partial
+// output) through distributed shared memory, each writing a slice of the bf16 output. No scratch
+// memory, one launch.
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdint>
 
 #include "common.cuh"
@@ -28,8 +31,9 @@ namespace svllm::k {
 namespace {
 
 constexpr int kThreads = 128;
-constexpr int kMaxSplits = 8;   // the portable cluster size
-constexpr int kMaxUnroll = 8;   // cache rows a lane has in flight (fewer when more CTAs must fit)
+constexpr int kWarps = kThreads / kWarpSize;
+constexpr int kMaxSplits = 8;  // the portable cluster size
+constexpr int kTileRows = 16;  // cache rows per tensor-core tile (the M of m16n8k16)
 
 struct AttnArgs {
   void* out;                 // [num_seqs, num_heads, head_dim] bf16, contiguous
@@ -42,9 +46,11 @@ struct AttnArgs {
   int64_t num_blocks;
   int max_blocks;
   int block_size;
+  uint32_t page_magic;       // j / block_size = (umulhi(j, page_magic) + j) >> page_shift
+  int page_shift;
   int num_kv_heads;
   int splits;
-  float scale;
+  float scale_log2;          // scale * log2(e): scores are kept in the base-2 exponent domain
   int* err;
 };
 
@@ -70,14 +76,61 @@ __device__ __forceinline__ float ld_remote_f32(const float* p, uint32_t rank) {
   return v;
 }
 
-template <int D, int G, int kUnroll>
+// 2^x (the ex2 instruction; 2^-inf = 0).
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// d += a * b on the tensor cores: A 16x16 bf16 (row), B 16x8 bf16 (col), fp32 accumulators.
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// The warp's 8x8 bf16 matrix (lane l holds row l / 4, columns 2 (l % 4) and 2 (l % 4) + 1)
+// transposed, in the same layout.
+__device__ __forceinline__ uint32_t transpose8x8(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+// Byte offset of cache row j of a request (its page looked up in the block table) from the
+// start of the cache. Division by the block size: multiply by a precomputed reciprocal and
+// shift (Granlund and Montgomery, "Division by invariant integers using multiplication", 1994,
+// exact for j < 2^31).
+__device__ __forceinline__ int64_t cache_row_offset(const AttnArgs& a, const int32_t* table,
+                                                    int j, int64_t row_bytes) {
+  const int page = static_cast<int>((__umulhi(static_cast<uint32_t>(j), a.page_magic) +
+                                     static_cast<uint32_t>(j)) >> a.page_shift);
+  int blk = __ldg(table + page);
+  if (static_cast<uint64_t>(blk) >= static_cast<uint64_t>(a.num_blocks)) {
+    raise_error(a.err, kErrBadIndex);  // an entry outside the cache: read block 0
+    blk = 0;
+  }
+  return (static_cast<int64_t>(blk) * a.block_size + (j - page * a.block_size)) * row_bytes;
+}
+
+// One CTA: one (request, KV head, context split); each warp a contiguous share of the split, in
+// tiles of 16 cache rows. Per tile, with lane l = 4 g + t:
+//   S^T[16 rows x 8 heads] = K[16 x D] . Q^T[D x 8]   (mma; lane loads rows g and g + 8)
+//   P^T = 2^(S^T * scale log2 e - running max), rounded to bf16, transposed by movmatrix into
+//         the B operand of
+//   O^T[D x 8 heads] += V^T[D x 16 rows] . P^T[16 x 8] (mma; V^T by movmatrix of the V rows)
+// The head dimension is permuted consistently inside each product: lane t's 16-byte piece c
+// of a row holds dims [32 c + 8 t, 32 c + 8 t + 8), which serve as the k-steps 2c and 2c + 1
+// of Q K^T and as four 8x8 blocks of V. Query heads beyond G are zero columns.
+template <int D, int G>
 __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnArgs a) {
   grid_dependency_sync();
-  constexpr int kLpr = D / 8;                  // lanes per cache row, 8 dims (16 bytes) each
-  constexpr int kGroups = kWarpSize / kLpr;    // rows one warp-wide load covers
-  constexpr int kStep = kGroups * kUnroll;     // rows per warp per iteration
-  constexpr int kWarps = kThreads / kWarpSize;
-  static_assert(kWarpSize % kLpr == 0, "a row's lanes stay in one warp");
+  constexpr int kPieces = D / 32;  // 16-byte pieces per lane per cache row
+  static_assert(G <= 8, "the query heads of a KV head fill at most the N = 8 of one mma");
 
   __shared__ float warp_m[kWarps][G], warp_l[kWarps][G];
   __shared__ float warp_acc[kWarps][G][D];
@@ -90,183 +143,188 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnAr
   const int kh = static_cast<int>(pair % a.num_kv_heads);
   const int warp = threadIdx.x / kWarpSize;
   const int lane = threadIdx.x % kWarpSize;
-  const int grp = lane / kLpr;  // which of the warp's kGroups rows this lane reads
-  const int sub = lane % kLpr;  // this lane's 8 dims: [8 sub, 8 sub + 8)
+  const int g = lane >> 2;  // the tile rows g and g + 8; query head g of the Q^T operand
+  const int t = lane & 3;   // dims 8t.. of each piece; query heads 2t, 2t + 1 of the results
 
   int seq_len = a.seq_lens[b];
   if (seq_len < 0 || seq_len > a.max_blocks * a.block_size) {  // past the block table
     if (threadIdx.x == 0) raise_error(a.err, kErrBadIndex);
     seq_len = seq_len < 0 ? 0 : a.max_blocks * a.block_size;
   }
-  // this CTA's split of the context, then this warp's contiguous share of it
-  const int chunk = (seq_len + a.splits - 1) / a.splits;
-  const int c_begin = min(seq_len, split * chunk);
-  const int c_end = min(seq_len, c_begin + chunk);
-  const int per_warp = (c_end - c_begin + kWarps - 1) / kWarps;
-  const int w_begin = min(c_end, c_begin + warp * per_warp);
-  const int w_end = min(c_end, w_begin + per_warp);
+  // this CTA's split of the context, then this warp's share of it, both in whole tiles
+  const int tiles = (seq_len + kTileRows - 1) / kTileRows;
+  const int split_tiles = (tiles + a.splits - 1) / a.splits;
+  const int warp_tiles = (split_tiles + kWarps - 1) / kWarps;
+  const int w_begin = min(seq_len, (split * split_tiles + warp * warp_tiles) * kTileRows);
+  const int w_end = min(seq_len, min((split + 1) * split_tiles,
+                                     split * split_tiles + (warp + 1) * warp_tiles) * kTileRows);
   const int32_t* table = a.block_tables + b * a.max_blocks;
 
-  // this lane's slice of each query head, fp32
-  float q[G][8];
+  // Q^T's B fragments: query head g of this KV head, this lane's dims of each piece
+  uint4 qf[kPieces];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
+  for (int c = 0; c < kPieces; ++c) qf[c] = make_uint4(0, 0, 0, 0);
+  if (g < G) {
     const uint8_t* qp = static_cast<const uint8_t*>(a.q) +
-                        (b * a.q_stride + static_cast<int64_t>(kh * G + g) * D + sub * 8) * 2;
-    float f[8];
-    unpack<Bf16>(ld_global_nc_v4(qp), f);
+                        (b * a.q_stride + static_cast<int64_t>(kh * G + g) * D + 8 * t) * 2;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) q[g][e] = f[e];
+    for (int c = 0; c < kPieces; ++c) qf[c] = ld_global_nc_v4(qp + 64 * c);
   }
 
-  float m[G], l[G], acc[G][8];
+  // O^T accumulators: m-tile (c, i) covers the blocks (c, 2i), (c, 2i + 1) of V's dims
+  float acc[kPieces][2][4];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = -__builtin_huge_valf();
-    l[g] = 0.0f;
+  for (int c = 0; c < kPieces; ++c) {
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[g][e] = 0.0f;
+    for (int i = 0; i < 2; ++i) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[c][i][e] = 0.0f;
+    }
   }
+  float m0 = -__builtin_huge_valf(), m1 = -__builtin_huge_valf();  // heads 2t, 2t + 1
+  float l0 = 0.0f, l1 = 0.0f;  // this lane's rows only; summed over the warp at the end
 
-  const int64_t row_elems = static_cast<int64_t>(a.num_kv_heads) * D;
-  const int64_t head_offset = static_cast<int64_t>(kh) * D + sub * 8;
-  const Bf16::Storage* kc = static_cast<const Bf16::Storage*>(a.k_cache);
-  const Bf16::Storage* vc = static_cast<const Bf16::Storage*>(a.v_cache);
+  const int64_t row_bytes = static_cast<int64_t>(a.num_kv_heads) * D * 2;
+  const uint8_t* kc = static_cast<const uint8_t*>(a.k_cache) + (static_cast<int64_t>(kh) * D + 8 * t) * 2;
+  const uint8_t* vc = static_cast<const uint8_t*>(a.v_cache) + (static_cast<int64_t>(kh) * D + 8 * t) * 2;
 
-  // Each iteration: kUnroll rows per lane, K and V loads all in flight together; the scores of
-  // the warp's kStep rows, their running max and sum by shuffles, then p * v into this lane's 8
-  // dims. No block-wide barrier until the warps meet at the end.
-  for (int r0 = w_begin; r0 < w_end; r0 += kStep) {
-    uint4 kraw[kUnroll], vraw[kUnroll];
+  for (int r0 = w_begin; r0 < w_end; r0 += kTileRows) {
+    const int j0 = r0 + g, j1 = r0 + g + 8;
+    const bool ok0 = j0 < w_end, ok1 = j1 < w_end;
+    const int64_t o0 = ok0 ? cache_row_offset(a, table, j0, row_bytes) : 0;
+    const int64_t o1 = ok1 ? cache_row_offset(a, table, j1, row_bytes) : 0;
+    uint4 k0[kPieces], k1[kPieces], v0[kPieces], v1[kPieces];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int j = r0 + u * kGroups + grp;
-      if (j < w_end) {
-        int blk = __ldg(table + j / a.block_size);
-        if (blk < 0 || blk >= a.num_blocks) {  // an entry outside the cache: read block 0
-          raise_error(a.err, kErrBadIndex);
-          blk = 0;
+    for (int c = 0; c < kPieces; ++c) {
+      k0[c] = ok0 ? ld_global_nc_v4(kc + o0 + 64 * c) : make_uint4(0, 0, 0, 0);
+      k1[c] = ok1 ? ld_global_nc_v4(kc + o1 + 64 * c) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int c = 0; c < kPieces; ++c) {  // rows past the share read as zeros: 0 * p, never NaN
+      v0[c] = ok0 ? ld_global_nc_v4(vc + o0 + 64 * c) : make_uint4(0, 0, 0, 0);
+      v1[c] = ok1 ? ld_global_nc_v4(vc + o1 + 64 * c) : make_uint4(0, 0, 0, 0);
+    }
+
+    // S^T: lane holds rows g, g + 8 x heads 2t, 2t + 1
+    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int c = 0; c < kPieces; ++c) {
+      mma_16816(s, k0[c].x, k1[c].x, k0[c].y, k1[c].y, qf[c].x, qf[c].y);
+      mma_16816(s, k0[c].z, k1[c].z, k0[c].w, k1[c].w, qf[c].z, qf[c].w);
+    }
+    const float x00 = ok0 ? s[0] * a.scale_log2 : -__builtin_huge_valf();
+    const float x01 = ok0 ? s[1] * a.scale_log2 : -__builtin_huge_valf();
+    const float x10 = ok1 ? s[2] * a.scale_log2 : -__builtin_huge_valf();
+    const float x11 = ok1 ? s[3] * a.scale_log2 : -__builtin_huge_valf();
+    float mx0 = fmaxf(x00, x10), mx1 = fmaxf(x01, x11);
+#pragma unroll
+    for (int off = 4; off < kWarpSize; off *= 2) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);  // finite: row r0 is valid
+    if (__any_sync(0xffffffffu, n0 > m0 || n1 > m1)) {    // the running max moved: rescale
+      const float al0 = exp2_approx(m0 - n0), al1 = exp2_approx(m1 - n1);
+      l0 *= al0;
+      l1 *= al1;
+#pragma unroll
+      for (int c = 0; c < kPieces; ++c) {
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          acc[c][i][0] *= al0;
+          acc[c][i][1] *= al1;
+          acc[c][i][2] *= al0;
+          acc[c][i][3] *= al1;
         }
-        const int64_t off = (static_cast<int64_t>(blk) * a.block_size + j % a.block_size) *
-                                row_elems + head_offset;
-        kraw[u] = ld_global_nc_v4(kc + off);
-        vraw[u] = ld_global_nc_v4(vc + off);
-      } else {
-        kraw[u] = make_uint4(0, 0, 0, 0);
-        vraw[u] = make_uint4(0, 0, 0, 0);
       }
+      m0 = n0;
+      m1 = n1;
     }
-    float s[kUnroll][G];
+    const float p00 = exp2_approx(x00 - m0), p01 = exp2_approx(x01 - m1);
+    const float p10 = exp2_approx(x10 - m0), p11 = exp2_approx(x11 - m1);
+    l0 += p00 + p10;
+    l1 += p01 + p11;
+    // P^T's B fragments: rows 2t, 2t + 1 (and + 8) of head g
+    const uint32_t pb0 = transpose8x8(pack_bf16x2(p00, p01));
+    const uint32_t pb1 = transpose8x8(pack_bf16x2(p10, p11));
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const bool valid = r0 + u * kGroups + grp < w_end;
-      float kf[8];
-      unpack<Bf16>(kraw[u], kf);
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float d = 0.0f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) d = __fmaf_rn(q[g][e], kf[e], d);
-#pragma unroll
-        for (int off = kLpr / 2; off > 0; off /= 2) d += __shfl_xor_sync(0xffffffffu, d, off);
-        s[u][g] = valid ? d * a.scale : -__builtin_huge_valf();
-      }
-    }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float mx = s[0][g];
-#pragma unroll
-      for (int u = 1; u < kUnroll; ++u) mx = fmaxf(mx, s[u][g]);
-#pragma unroll
-      for (int off = kLpr; off < kWarpSize; off *= 2) {
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      }
-      const float m_new = fmaxf(m[g], mx);  // finite: the iteration has a valid row
-      const float alpha = __expf(m[g] - m_new);
-      float ps = 0.0f;
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        s[u][g] = __expf(s[u][g] - m_new);  // 0 for rows past the share
-        ps += s[u][g];
-      }
-#pragma unroll
-      for (int off = kLpr; off < kWarpSize; off *= 2) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-      l[g] = l[g] * alpha + ps;
-      m[g] = m_new;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[g][e] *= alpha;
-    }
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      float vf[8];
-      unpack<Bf16>(vraw[u], vf);
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[g][e] = __fmaf_rn(s[u][g], vf[e], acc[g][e]);
-      }
+    for (int c = 0; c < kPieces; ++c) {
+      mma_16816(acc[c][0], transpose8x8(v0[c].x), transpose8x8(v0[c].y), transpose8x8(v1[c].x),
+                transpose8x8(v1[c].y), pb0, pb1);
+      mma_16816(acc[c][1], transpose8x8(v0[c].z), transpose8x8(v0[c].w), transpose8x8(v1[c].z),
+                transpose8x8(v1[c].w), pb0, pb1);
     }
   }
-  // the warp's row groups hold partial sums of the same dims: add them up
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
+  for (int off = 4; off < kWarpSize; off *= 2) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  const int h0 = 2 * t, h1 = 2 * t + 1;
+  if (g == 0) {
+    if (h0 < G) {
+      warp_m[warp][h0] = m0;
+      warp_l[warp][h0] = l0;
+    }
+    if (h1 < G) {
+      warp_m[warp][h1] = m1;
+      warp_l[warp][h1] = l1;
+    }
+  }
+  // O^T element (dim, head): m-tile (c, i) row g is dim 32c + 8(g/2) + 4i + g%2, row g + 8
+  // that dim + 2 (block (c, j) column 2t' + e is dim 32c + 8t' + 2j + e)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
+  for (int c = 0; c < kPieces; ++c) {
 #pragma unroll
-      for (int off = kLpr; off < kWarpSize; off *= 2) {
-        acc[g][e] += __shfl_xor_sync(0xffffffffu, acc[g][e], off);
+    for (int i = 0; i < 2; ++i) {
+      const int d = 32 * c + 8 * (g >> 1) + 4 * i + (g & 1);
+      if (h0 < G) {
+        warp_acc[warp][h0][d] = acc[c][i][0];
+        warp_acc[warp][h0][d + 2] = acc[c][i][2];
       }
-    }
-  }
-  if (grp == 0) {
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) warp_acc[warp][g][sub * 8 + e] = acc[g][e];
-    }
-  }
-  if (lane == 0) {
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      warp_m[warp][g] = m[g];
-      warp_l[warp][g] = l[g];
+      if (h1 < G) {
+        warp_acc[warp][h1][d] = acc[c][i][1];
+        warp_acc[warp][h1][d + 2] = acc[c][i][3];
+      }
     }
   }
   __syncthreads();
   // the warps' (max, sum, partial) merged into the CTA's
   if (threadIdx.x < G) {
-    const int g = threadIdx.x;
-    float mx = warp_m[0][g];
+    const int h = threadIdx.x;
+    float mx = warp_m[0][h];
 #pragma unroll
-    for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, warp_m[w][g]);
+    for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, warp_m[w][h]);
     float ls = 0.0f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
-      ls += warp_m[w][g] == -__builtin_huge_valf() ? 0.0f : warp_l[w][g] * __expf(warp_m[w][g] - mx);
+      ls += warp_m[w][h] == -__builtin_huge_valf() ? 0.0f
+                                                   : warp_l[w][h] * exp2_approx(warp_m[w][h] - mx);
     }
-    m_sm[g] = mx;
-    l_sm[g] = ls;
+    m_sm[h] = mx;
+    l_sm[h] = ls;
   }
   for (int idx = threadIdx.x; idx < G * D; idx += kThreads) {
-    const int g = idx / D, d = idx % D;
-    float mx = warp_m[0][g];
+    const int h = idx / D, d = idx % D;
+    float mx = warp_m[0][h];
 #pragma unroll
-    for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, warp_m[w][g]);
+    for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, warp_m[w][h]);
     float o = 0.0f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
-      o += warp_m[w][g] == -__builtin_huge_valf() ? 0.0f
-                                                    : warp_acc[w][g][d] * __expf(warp_m[w][g] - mx);
+      o += warp_m[w][h] == -__builtin_huge_valf()
+               ? 0.0f
+               : warp_acc[w][h][d] * exp2_approx(warp_m[w][h] - mx);
     }
-    part[g][d] = o;
+    part[h][d] = o;
   }
   __syncthreads();
 
   __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + (b * a.num_kv_heads + kh) * G * D;
   if (a.splits == 1) {
     for (int idx = threadIdx.x; idx < G * D; idx += kThreads) {
-      const int g = idx / D;
-      out[idx] = __float2bfloat16_rn(l_sm[g] > 0.0f ? part[g][idx % D] / l_sm[g] : 0.0f);
+      const int h = idx / D;
+      out[idx] = __float2bfloat16_rn(l_sm[h] > 0.0f ? part[h][idx % D] / l_sm[h] : 0.0f);
     }
     return;
   }
@@ -276,14 +334,14 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnAr
   const int per = G * D / a.splits;
   const int first = static_cast<int>(cluster_rank()) * per;
   for (int idx = first + threadIdx.x; idx < first + per; idx += kThreads) {
-    const int g = idx / D, d = idx % D;
+    const int h = idx / D, d = idx % D;
     float mr[kMaxSplits], lr[kMaxSplits], pr[kMaxSplits];
 #pragma unroll
     for (int r = 0; r < kMaxSplits; ++r) {
       if (r < a.splits) {
-        mr[r] = ld_remote_f32(&m_sm[g], r);
-        lr[r] = ld_remote_f32(&l_sm[g], r);
-        pr[r] = ld_remote_f32(&part[g][d], r);
+        mr[r] = ld_remote_f32(&m_sm[h], r);
+        lr[r] = ld_remote_f32(&l_sm[h], r);
+        pr[r] = ld_remote_f32(&part[h][d], r);
       }
     }
     float mx = -__builtin_huge_valf();
@@ -295,7 +353,7 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnAr
 #pragma unroll
     for (int r = 0; r < kMaxSplits; ++r) {
       if (r < a.splits) {
-        const float w = mr[r] == -__builtin_huge_valf() ? 0.0f : __expf(mr[r] - mx);
+        const float w = mr[r] == -__builtin_huge_valf() ? 0.0f : exp2_approx(mr[r] - mx);
         o += w * pr[r];
         lsum += w * lr[r];
       }
@@ -305,33 +363,22 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnAr
   cluster_sync_all();  // every CTA's shared memory stays valid until the others have read it
 }
 
-// Rows in flight per lane: 8 while every CTA of the launch is resident at once (each warp's
-// latency chain is then what bounds it), 4 when the CTAs run in waves (then occupancy does);
-// half of that with 8 query heads per KV head, whose accumulators take the registers. Measured
-// on a B200: 64 requests x 512 tokens 36 us at 8 rows, 44 us at 4; 256 requests 141 vs 128 us.
 template <int D, int G>
-int launch_attention(const AttnArgs& a, int64_t num_seqs, int device, cudaStream_t stream) {
-  constexpr int kDeep = G >= 8 ? kMaxUnroll / 2 : kMaxUnroll;
+int launch_attention(const AttnArgs& a, int64_t num_seqs, cudaStream_t stream) {
   const int64_t blocks = num_seqs * a.num_kv_heads * a.splits;
   const unsigned cluster = a.splits > 1 ? static_cast<unsigned>(a.splits) : 1u;
-  const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(decode_attention_kernel<D, G, kDeep>),
-                                   kThreads, 0, device);
-  if (blocks <= static_cast<int64_t>(sm_count(device)) * (per_sm > 0 ? per_sm : 1)) {
-    return launch(decode_attention_kernel<D, G, kDeep>, dim3(static_cast<unsigned>(blocks)),
-                  dim3(kThreads), 0, stream, cluster, a);
-  }
-  return launch(decode_attention_kernel<D, G, kDeep / 2>, dim3(static_cast<unsigned>(blocks)),
-                dim3(kThreads), 0, stream, cluster, a);
+  // not scheduled early behind the previous kernel: its CTAs take all of an SM's registers
+  return launch_serialized(decode_attention_kernel<D, G>, dim3(static_cast<unsigned>(blocks)),
+                           dim3(kThreads), 0, stream, cluster, a);
 }
 
 template <int D>
-int dispatch_group(const AttnArgs& a, int64_t num_seqs, int group, int device,
-                   cudaStream_t stream) {
+int dispatch_group(const AttnArgs& a, int64_t num_seqs, int group, cudaStream_t stream) {
   switch (group) {
-    case 1: return launch_attention<D, 1>(a, num_seqs, device, stream);
-    case 2: return launch_attention<D, 2>(a, num_seqs, device, stream);
-    case 4: return launch_attention<D, 4>(a, num_seqs, device, stream);
-    case 8: return launch_attention<D, 8>(a, num_seqs, device, stream);
+    case 1: return launch_attention<D, 1>(a, num_seqs, stream);
+    case 2: return launch_attention<D, 2>(a, num_seqs, stream);
+    case 4: return launch_attention<D, 4>(a, num_seqs, stream);
+    case 8: return launch_attention<D, 8>(a, num_seqs, stream);
     default: return SVLLM_ERR_UNSUPPORTED;
   }
 }
@@ -378,8 +425,16 @@ extern "C" int svllm_paged_decode_attention_bf16(
   a.num_blocks = num_blocks;
   a.max_blocks = static_cast<int>(max_blocks);
   a.block_size = static_cast<int>(block_size);
+  // the reciprocal of the block size for the page lookup: shift = ceil(log2 block_size),
+  // magic = floor(2^32 (2^shift - block_size) / block_size) + 1
+  int shift = 0;
+  while ((int64_t{1} << shift) < block_size) ++shift;
+  a.page_shift = shift;
+  a.page_magic = static_cast<uint32_t>(
+      ((uint64_t{1} << 32) * ((uint64_t{1} << shift) - static_cast<uint64_t>(block_size))) /
+          static_cast<uint64_t>(block_size) + 1);
   a.num_kv_heads = static_cast<int>(num_kv_heads);
-  a.scale = scale;
+  a.scale_log2 = static_cast<float>(static_cast<double>(scale) / std::log(2.0));
   a.err = err;
   // Split the context until there are about two CTAs per SM, never below 64 tokens per split.
   const int64_t pairs = num_seqs * num_kv_heads;
@@ -390,6 +445,6 @@ extern "C" int svllm_paged_decode_attention_bf16(
   while (pow2 * 2 <= splits && pow2 * 2 <= kMaxSplits) pow2 *= 2;
   a.splits = pow2;
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return head_dim == 128 ? dispatch_group<128>(a, num_seqs, static_cast<int>(group), device, s)
-                         : dispatch_group<64>(a, num_seqs, static_cast<int>(group), device, s);
+  return head_dim == 128 ? dispatch_group<128>(a, num_seqs, static_cast<int>(group), s)
+                         : dispatch_group<64>(a, num_seqs, static_cast<int>(group), s);
 }
