@@ -89,14 +89,16 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload",
                    choices=sorted(WORKLOADS) + ["sampling", "lm-head", "model-decode",
-                                                "decode-attention"],
+                                                "decode-attention", "decode-linear"],
                    default="sweep",
                    help="sampling: greedy argmax over [tokens, 151936] bf16 logits (one op, "
                         "not the chain); lm-head: the tied LM head fused with greedy sampling "
                         "(one tcgen05 kernel) beside matmul + argmax; model-decode: Qwen3-0.6B "
                         "decode steps through the model forward, eager and from CUDA graphs; "
                         "decode-attention: the paged decode-attention kernel of one Qwen3-0.6B "
-                        "layer beside the gather + SDPA composite it replaces")
+                        "layer beside the gather + SDPA composite it replaces; decode-linear: "
+                        "the Qwen3-0.6B projections at decode batch sizes, the decode-linear "
+                        "kernel beside torch.matmul (cuBLAS)")
     p.add_argument("--batches", default="1,8,64,256",
                    help="model-decode: comma-separated decode batch sizes")
     p.add_argument("--context", type=int, default=512,
@@ -714,6 +716,85 @@ def run_decode_attention(args) -> int:
     return 0
 
 
+def run_decode_linear(args) -> int:
+    """The four projections of a Qwen3-0.6B layer (qkv, o, gate_up, down) at each `--batches`
+    size up to 16 rows, through the C ABI (svllm_decode_linear_bf16), beside torch.matmul
+    (cuBLAS) on the same operands. At these sizes the work is a stream over the weight: the
+    roofline is HBM bandwidth on the weight bytes (plus the activations in and out)."""
+    import torch
+
+    import svllm_capi as capi
+
+    cfg = QWEN3
+    h, d = cfg["hidden"], cfg["head_dim"]
+    shapes = {"qkv": ((cfg["heads"] + 2 * cfg["kv_heads"]) * d, h),
+              "o_proj": (h, cfg["heads"] * d), "gate_up": (2 * cfg["inter"], h),
+              "down": (h, cfg["inter"])}
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(17)
+    peaks = measured_peaks()
+
+    def replay_us(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(args.steps):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        graph.replay()
+        stop.record()
+        torch.cuda.synchronize()
+        return start.elapsed_time(stop) / args.steps * 1e3
+
+    # one weight per step of the replay, so that consecutive launches do not find it in L2
+    copies = max(2, -(-256 * 2 ** 20 // min(n * k * 2 for n, k in shapes.values())))
+    for name, (n, k) in shapes.items():
+        ws = [(torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+              for _ in range(copies)]
+        for b in [int(x) for x in args.batches.split(",") if int(x) <= 16]:
+            x = torch.randn(b, k, device=dev, generator=g).to(torch.bfloat16)
+            out = torch.empty(b, n, device=dev, dtype=torch.bfloat16)
+            it = {"i": 0}
+
+            def ours():
+                capi.decode_linear(out, x, ws[it["i"] % copies])
+                it["i"] += 1
+
+            def cublas():
+                torch.matmul(x, ws[it["i"] % copies].t())
+                it["i"] += 1
+
+            us = replay_us(ours)
+            ref_us = replay_us(cublas)
+            capi.decode_linear(out, x, ws[0])
+            err = float((out.float() - (x.float() @ ws[0].float().t())).abs().max())
+            traffic = n * k * 2 + b * k * 2 + b * n * 2
+            gbs = traffic / (us * 1e-6) / 1e9
+            print(json.dumps({
+                "metric": "decode linear (weight bytes streamed per second)",
+                "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(us / 1e3, 5),
+                "us_per_launch": round(us, 2), "higher_is_better": True,
+                "dtype": "bf16 (fp32 accumulation)", "data": "synthetic",
+                "config": {"workload": f"Qwen3-0.6B {name} projection", "rows": b,
+                           "out_features": n, "in_features": k, "weight_copies": copies,
+                           "timing": "CUDA graph replay, a different weight copy per launch "
+                                     "(the copies exceed L2)"},
+                "roofline": {"bound": "hbm", "achieved": round(gbs, 1),
+                             "peak": float(peaks["hbm_gbs"]), "unit": "GB/s",
+                             "frac": round(gbs / float(peaks["hbm_gbs"]), 4)},
+                "cublas_us": round(ref_us, 2), "speedup": round(ref_us / us, 3),
+                "max_abs_err_vs_fp32": round(err, 6), "gpu_launches": args.steps}),
+                flush=True)
+        del ws
+    return 0
+
+
 def main() -> int:
     args = parse_args()
     if args.workload == "sampling":
@@ -724,6 +805,8 @@ def main() -> int:
         return run_lm_head(args)
     if args.workload == "decode-attention":
         return run_decode_attention(args)
+    if args.workload == "decode-linear":
+        return run_decode_linear(args)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)

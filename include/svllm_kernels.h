@@ -279,6 +279,20 @@ int svllm_paged_decode_attention_bf16(void* out, const void* q, int64_t q_token_
                                       int64_t max_seq_len, float scale, svllm_stream stream);
 
 /*
+ * A linear layer at decode batch sizes: out[r, n] = bf16(sum_k x[r, k] * weight[n, k]) for
+ * r < num_rows <= 16 (the weight streamed into tensor-core registers, fp32 accumulation, one
+ * rounding to bf16). x: [num_rows, in_features] bf16 at x_stride elements; weight:
+ * [out_features, in_features] bf16 at weight_stride elements (a checkpoint's projection, no
+ * bias); out: [num_rows, out_features] bf16 at out_stride elements. More than 16 rows,
+ * in_features not a multiple of 8, or x or weight not 16-byte aligned with strides of whole 16
+ * bytes: SVLLM_ERR_UNSUPPORTED, and the caller's GEMM serves the call. Replaces, for decode
+ * steps, at::linear in the model forward the reference plans (src/model, docs/ROADMAP.md:24-25).
+ */
+int svllm_decode_linear_bf16(void* out, int64_t out_stride, const void* x, int64_t num_rows,
+                             int64_t in_features, int64_t x_stride, const void* weight,
+                             int64_t out_features, int64_t weight_stride, svllm_stream stream);
+
+/*
  * svllm_lm_head_argmax_bf16 without a workspace argument, for callers that cannot allocate
  * device memory: a host program driving this C ABI through an FFI with no CUDA allocator of its
  * own, or one whose device memory is all owned by another allocator. It allocates nothing; the

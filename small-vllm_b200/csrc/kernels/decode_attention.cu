@@ -54,28 +54,6 @@ struct AttnArgs {
   int* err;
 };
 
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
-               ::: "memory");
-}
-
-// A float of cluster CTA `rank`'s shared memory at the address of `p` in this CTA's. Not
-// volatile: the loads of a merge are independent and may be in flight together (the cluster
-// barrier before them orders them after the writes).
-__device__ __forceinline__ float ld_remote_f32(const float* p, uint32_t rank) {
-  uint32_t addr;
-  asm("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(addr) : "r"(smem_addr(p)), "r"(rank));
-  float v;
-  asm("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
-  return v;
-}
-
 // 2^x (the ex2 instruction; 2^-inf = 0).
 __device__ __forceinline__ float exp2_approx(float x) {
   float y;

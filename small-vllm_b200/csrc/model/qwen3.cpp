@@ -35,6 +35,27 @@ at::Tensor weight(const std::unordered_map<std::string, at::Tensor>& weights,
   return it->second;
 }
 
+// x [T, K] . w [N, K]^T. Decode-sized batches (up to 16 rows) in bf16 on CUDA take the
+// decode-linear kernel, which streams the weight over every SM; larger batches, other dtypes,
+// the CPU and shapes that kernel does not take go through at::linear (cuBLAS on GPU).
+at::Tensor project(const at::Tensor& x, const at::Tensor& w) {
+#ifdef SVLLM_CUDA
+  if (x.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+      x.dim() == 2 && w.dim() == 2 && x.size(0) <= 16 && x.stride(1) == 1 && w.stride(1) == 1) {
+    at::Tensor out = at::empty({x.size(0), w.size(0)}, x.options());
+    const c10::cuda::CUDAGuard device_guard(x.device());
+    const int status = svllm_decode_linear_bf16(
+        out.data_ptr(), out.stride(0), x.data_ptr(), x.size(0), x.size(1), x.stride(0),
+        w.data_ptr(), w.size(0), w.stride(0),
+        reinterpret_cast<svllm_stream>(c10::cuda::getCurrentCUDAStream().stream()));
+    if (status == SVLLM_OK) return out;
+    TORCH_CHECK(status == SVLLM_ERR_UNSUPPORTED, "Model: decode linear: ",
+                svllm_status_string(status));
+  }
+#endif
+  return at::linear(x, w);
+}
+
 }  // namespace
 
 Model::Model(const ModelConfig& config,
@@ -190,7 +211,7 @@ at::Tensor Model::forward(const at::Tensor& ids, const at::Tensor& positions,
     } else {
       ops::add_rms_norm(hidden, residual, layer.input_norm, eps);
     }
-    const at::Tensor qkv = at::linear(hidden, layer.qkv);  // [T, (Hq + 2 Hk) D]
+    const at::Tensor qkv = project(hidden, layer.qkv);  // [T, (Hq + 2 Hk) D]
     const at::Tensor q = qkv.narrow(1, 0, Hq * D).view({T, Hq, D});
     const at::Tensor k = qkv.narrow(1, Hq * D, Hk * D).view({T, Hk, D});
     const at::Tensor v = qkv.narrow(1, (Hq + Hk) * D, Hk * D).view({T, Hk, D});
@@ -204,9 +225,9 @@ at::Tensor Model::forward(const at::Tensor& ids, const at::Tensor& positions,
     }
     const at::Tensor attn = paged ? paged_decode_attention(q, static_cast<int64_t>(l), meta)
                                   : attention(q, static_cast<int64_t>(l), plan);
-    hidden = at::linear(attn, layer.o_proj);
+    hidden = project(attn, layer.o_proj);
     ops::add_rms_norm(hidden, residual, layer.post_norm, eps);
-    hidden = at::linear(ops::silu_and_mul(at::linear(hidden, layer.gate_up)), layer.down);
+    hidden = project(ops::silu_and_mul(project(hidden, layer.gate_up)), layer.down);
   }
   ops::add_rms_norm(hidden, residual, final_norm_, eps);
   return hidden;

@@ -8,9 +8,10 @@
 // Per layer: add_rms_norm -> one qkv GEMM -> qk_norm_rope_cache (Qwen3) or rope_cache (Llama),
 // which also writes k and v into the paged cache -> attention over the cache -> o GEMM ->
 // add_rms_norm -> one gate_up GEMM -> silu_and_mul -> down GEMM. GEMMs are torch::linear
-// (cuBLAS on GPU, as the reference plans, docs/ROADMAP.md:16). Attention: on CUDA decode steps
-// the paged decode-attention kernel reads the cache in place; otherwise (prefill, mixed steps,
-// CPU) a LibTorch composite over the gathered cache.
+// (cuBLAS on GPU, as the reference plans, docs/ROADMAP.md:16), except for batches of up to 16
+// token rows on CUDA, which take this library's decode-linear kernel. Attention: on CUDA
+// decode steps the paged decode-attention kernel reads the cache in place; otherwise (prefill,
+// mixed steps, CPU) a LibTorch composite over the gathered cache.
 
 #include <ATen/ATen.h>
 

@@ -69,6 +69,7 @@ SIGNATURES = {
     "svllm_lm_head_argmax_static_bf16": [_P, _I64, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P],
     "svllm_paged_decode_attention_bf16": [_P, _P, _I64, _P, _P, _I64, _I64, _P, _I64, _P, _I64,
                                           _I64, _I64, _I64, _I64, ctypes.c_float, _P],
+    "svllm_decode_linear_bf16": [_P, _I64, _P, _I64, _I64, _I64, _P, _I64, _I64, _P],
     "svllm_read_device_error": [_I, _I, _P],
     "svllm_set_pipeline": [ctypes.c_char_p, _I64, _I64, _I64],
 }
@@ -255,6 +256,15 @@ def paged_decode_attention(out, q, k_cache, v_cache, block_tables, seq_lens, max
         num_blocks, block_size, block_tables.data_ptr(), block_tables.shape[1],
         seq_lens.data_ptr(), num_seqs, num_heads, num_kv_heads, head_dim, max_seq_len, scale,
         _stream(stream)), "paged_decode_attention")
+
+
+def decode_linear(out, x, weight, stream=None) -> None:
+    """out [R, N] = x [R, K] . weight [N, K]^T for R <= 16 (bf16, fp32 accumulation)."""
+    rows, in_features, x_stride = _rows(x)
+    out_features, _, weight_stride = _rows(weight)
+    check(lib().svllm_decode_linear_bf16(
+        out.data_ptr(), out.stride(0), x.data_ptr(), rows, in_features, x_stride,
+        weight.data_ptr(), out_features, weight_stride, _stream(stream)), "decode_linear")
 
 
 def read_device_error(device: int = 0, reset: bool = True) -> int:
