@@ -9,8 +9,8 @@
 // steps, the gather-then-SDPA composite of the model forward; the reference plans the kernel
 // ("Decode attention: Split-KV paged kernel, GQA-aware", docs/ROADMAP.md).
 //
-// A CTA of 128 threads owns (request, KV head, context split), and each of its 4 warps a
-// contiguous share of that split, in tiles of 16 cache rows. Both products of a tile run on the
+// A CTA of 4 warps (8 or 16 when the grid is small) owns (request, KV head, context split), and
+// each warp a contiguous share of that split, in tiles of 16 cache rows. Both products of a tile run on the
 // tensor cores (mma.sync m16n8k16, bf16 in, fp32 accumulate), with the query heads of the KV
 // head as the N = 8 columns: S^T = K Q^T straight from the rows a lane loads, then P^T (the
 // tile's softmax numerators, rounded to bf16 as flash attention does) and V^T transposed in
@@ -30,8 +30,6 @@
 namespace svllm::k {
 namespace {
 
-constexpr int kThreads = 128;
-constexpr int kWarps = kThreads / kWarpSize;
 constexpr int kMaxSplits = 8;  // the portable cluster size
 constexpr int kTileRows = 16;  // cache rows per tensor-core tile (the M of m16n8k16)
 
@@ -104,8 +102,9 @@ __device__ __forceinline__ int64_t cache_row_offset(const AttnArgs& a, const int
 // The head dimension is permuted consistently inside each product: lane t's 16-byte piece c
 // of a row holds dims [32 c + 8 t, 32 c + 8 t + 8), which serve as the k-steps 2c and 2c + 1
 // of Q K^T and as four 8x8 blocks of V. Query heads beyond G are zero columns.
-template <int D, int G>
-__global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnArgs a) {
+template <int D, int G, int kWarps>
+__global__ void __launch_bounds__(kWarps * kWarpSize) decode_attention_kernel(const AttnArgs a) {
+  constexpr int kThreads = kWarps * kWarpSize;
   grid_dependency_sync();
   constexpr int kPieces = D / 32;  // 16-byte pieces per lane per cache row
   static_assert(G <= 8, "the query heads of a KV head fill at most the N = 8 of one mma");
@@ -166,41 +165,47 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnAr
   const uint8_t* kc = static_cast<const uint8_t*>(a.k_cache) + (static_cast<int64_t>(kh) * D + 8 * t) * 2;
   const uint8_t* vc = static_cast<const uint8_t*>(a.v_cache) + (static_cast<int64_t>(kh) * D + 8 * t) * 2;
 
-  for (int r0 = w_begin; r0 < w_end; r0 += kTileRows) {
-    const int j0 = r0 + g, j1 = r0 + g + 8;
-    const bool ok0 = j0 < w_end, ok1 = j1 < w_end;
-    const int64_t o0 = ok0 ? cache_row_offset(a, table, j0, row_bytes) : 0;
-    const int64_t o1 = ok1 ? cache_row_offset(a, table, j1, row_bytes) : 0;
+  // One tile: rows r0 + g and r0 + g + 8 of this lane, K and V, all pieces.
+  struct Tile {
     uint4 k0[kPieces], k1[kPieces], v0[kPieces], v1[kPieces];
+    bool ok0, ok1;
+  };
+  const auto load = [&](Tile& tl, int r0) {
+    const int j0 = r0 + g, j1 = r0 + g + 8;
+    tl.ok0 = j0 < w_end;
+    tl.ok1 = j1 < w_end;
+    const int64_t o0 = tl.ok0 ? cache_row_offset(a, table, j0, row_bytes) : 0;
+    const int64_t o1 = tl.ok1 ? cache_row_offset(a, table, j1, row_bytes) : 0;
 #pragma unroll
     for (int c = 0; c < kPieces; ++c) {
-      k0[c] = ok0 ? ld_global_nc_v4(kc + o0 + 64 * c) : make_uint4(0, 0, 0, 0);
-      k1[c] = ok1 ? ld_global_nc_v4(kc + o1 + 64 * c) : make_uint4(0, 0, 0, 0);
+      tl.k0[c] = tl.ok0 ? ld_global_nc_v4(kc + o0 + 64 * c) : make_uint4(0, 0, 0, 0);
+      tl.k1[c] = tl.ok1 ? ld_global_nc_v4(kc + o1 + 64 * c) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int c = 0; c < kPieces; ++c) {  // rows past the share read as zeros: 0 * p, never NaN
-      v0[c] = ok0 ? ld_global_nc_v4(vc + o0 + 64 * c) : make_uint4(0, 0, 0, 0);
-      v1[c] = ok1 ? ld_global_nc_v4(vc + o1 + 64 * c) : make_uint4(0, 0, 0, 0);
+      tl.v0[c] = tl.ok0 ? ld_global_nc_v4(vc + o0 + 64 * c) : make_uint4(0, 0, 0, 0);
+      tl.v1[c] = tl.ok1 ? ld_global_nc_v4(vc + o1 + 64 * c) : make_uint4(0, 0, 0, 0);
     }
-
+  };
+  const auto process = [&](const Tile& tl) {
     // S^T: lane holds rows g, g + 8 x heads 2t, 2t + 1
     float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int c = 0; c < kPieces; ++c) {
-      mma_16816(s, k0[c].x, k1[c].x, k0[c].y, k1[c].y, qf[c].x, qf[c].y);
-      mma_16816(s, k0[c].z, k1[c].z, k0[c].w, k1[c].w, qf[c].z, qf[c].w);
+      mma_16816(s, tl.k0[c].x, tl.k1[c].x, tl.k0[c].y, tl.k1[c].y, qf[c].x, qf[c].y);
+      mma_16816(s, tl.k0[c].z, tl.k1[c].z, tl.k0[c].w, tl.k1[c].w, qf[c].z, qf[c].w);
     }
-    const float x00 = ok0 ? s[0] * a.scale_log2 : -__builtin_huge_valf();
-    const float x01 = ok0 ? s[1] * a.scale_log2 : -__builtin_huge_valf();
-    const float x10 = ok1 ? s[2] * a.scale_log2 : -__builtin_huge_valf();
-    const float x11 = ok1 ? s[3] * a.scale_log2 : -__builtin_huge_valf();
+    const float x00 = tl.ok0 ? s[0] * a.scale_log2 : -__builtin_huge_valf();
+    const float x01 = tl.ok0 ? s[1] * a.scale_log2 : -__builtin_huge_valf();
+    const float x10 = tl.ok1 ? s[2] * a.scale_log2 : -__builtin_huge_valf();
+    const float x11 = tl.ok1 ? s[3] * a.scale_log2 : -__builtin_huge_valf();
     float mx0 = fmaxf(x00, x10), mx1 = fmaxf(x01, x11);
 #pragma unroll
     for (int off = 4; off < kWarpSize; off *= 2) {
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
     }
-    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);  // finite: row r0 is valid
+    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);  // finite: the tile's first row is valid
     if (__any_sync(0xffffffffu, n0 > m0 || n1 > m1)) {    // the running max moved: rescale
       const float al0 = exp2_approx(m0 - n0), al1 = exp2_approx(m1 - n1);
       l0 *= al0;
@@ -227,11 +232,17 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnAr
     const uint32_t pb1 = transpose8x8(pack_bf16x2(p10, p11));
 #pragma unroll
     for (int c = 0; c < kPieces; ++c) {
-      mma_16816(acc[c][0], transpose8x8(v0[c].x), transpose8x8(v0[c].y), transpose8x8(v1[c].x),
-                transpose8x8(v1[c].y), pb0, pb1);
-      mma_16816(acc[c][1], transpose8x8(v0[c].z), transpose8x8(v0[c].w), transpose8x8(v1[c].z),
-                transpose8x8(v1[c].w), pb0, pb1);
+      mma_16816(acc[c][0], transpose8x8(tl.v0[c].x), transpose8x8(tl.v0[c].y),
+                transpose8x8(tl.v1[c].x), transpose8x8(tl.v1[c].y), pb0, pb1);
+      mma_16816(acc[c][1], transpose8x8(tl.v0[c].z), transpose8x8(tl.v0[c].w),
+                transpose8x8(tl.v1[c].z), transpose8x8(tl.v1[c].w), pb0, pb1);
     }
+  };
+
+  for (int r0 = w_begin; r0 < w_end; r0 += kTileRows) {
+    Tile tl;
+    load(tl, r0);
+    process(tl);
   }
 #pragma unroll
   for (int off = 4; off < kWarpSize; off *= 2) {
@@ -341,22 +352,40 @@ __global__ void __launch_bounds__(kThreads) decode_attention_kernel(const AttnAr
   cluster_sync_all();  // every CTA's shared memory stays valid until the others have read it
 }
 
+// Warps per CTA: 4 when the grid fills the SMs several times over; more when it is small
+// (decode of a few requests), so that each SM still has enough cache rows in flight, but no
+// more than the split has tiles of 16 rows, and at most what keeps the warps' partial outputs
+// within 40 KB of shared memory. Measured on a B200 (one Qwen3-0.6B layer): one request of
+// 2048 tokens 8.0 -> 7.0 us with 16 warps, 8 requests 14.6 -> 12.2 us with 8.
 template <int D, int G>
-int launch_attention(const AttnArgs& a, int64_t num_seqs, cudaStream_t stream) {
+int launch_attention(const AttnArgs& a, int64_t num_seqs, int64_t split_tiles, int device,
+                     cudaStream_t stream) {
+  constexpr int kMaxWarps = 40960 / (G * D * 4) >= 16 ? 16 : 40960 / (G * D * 4) >= 8 ? 8 : 4;
   const int64_t blocks = num_seqs * a.num_kv_heads * a.splits;
+  const int64_t sms = sm_count(device);
   const unsigned cluster = a.splits > 1 ? static_cast<unsigned>(a.splits) : 1u;
+  const dim3 grid(static_cast<unsigned>(blocks));
   // not scheduled early behind the previous kernel: its CTAs take all of an SM's registers
-  return launch_serialized(decode_attention_kernel<D, G>, dim3(static_cast<unsigned>(blocks)),
-                           dim3(kThreads), 0, stream, cluster, a);
+  if (kMaxWarps >= 16 && blocks <= sms && split_tiles >= 16) {
+    return launch_serialized(decode_attention_kernel<D, G, (kMaxWarps >= 16 ? 16 : 4)>, grid,
+                             dim3((kMaxWarps >= 16 ? 16 : 4) * kWarpSize), 0, stream, cluster, a);
+  }
+  if (kMaxWarps >= 8 && blocks <= 2 * sms && split_tiles >= 8) {
+    return launch_serialized(decode_attention_kernel<D, G, (kMaxWarps >= 8 ? 8 : 4)>, grid,
+                             dim3((kMaxWarps >= 8 ? 8 : 4) * kWarpSize), 0, stream, cluster, a);
+  }
+  return launch_serialized(decode_attention_kernel<D, G, 4>, grid, dim3(4 * kWarpSize), 0, stream,
+                           cluster, a);
 }
 
 template <int D>
-int dispatch_group(const AttnArgs& a, int64_t num_seqs, int group, cudaStream_t stream) {
+int dispatch_group(const AttnArgs& a, int64_t num_seqs, int64_t split_tiles, int group,
+                   int device, cudaStream_t stream) {
   switch (group) {
-    case 1: return launch_attention<D, 1>(a, num_seqs, stream);
-    case 2: return launch_attention<D, 2>(a, num_seqs, stream);
-    case 4: return launch_attention<D, 4>(a, num_seqs, stream);
-    case 8: return launch_attention<D, 8>(a, num_seqs, stream);
+    case 1: return launch_attention<D, 1>(a, num_seqs, split_tiles, device, stream);
+    case 2: return launch_attention<D, 2>(a, num_seqs, split_tiles, device, stream);
+    case 4: return launch_attention<D, 4>(a, num_seqs, split_tiles, device, stream);
+    case 8: return launch_attention<D, 8>(a, num_seqs, split_tiles, device, stream);
     default: return SVLLM_ERR_UNSUPPORTED;
   }
 }
@@ -423,6 +452,9 @@ extern "C" int svllm_paged_decode_attention_bf16(
   while (pow2 * 2 <= splits && pow2 * 2 <= kMaxSplits) pow2 *= 2;
   a.splits = pow2;
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return head_dim == 128 ? dispatch_group<128>(a, num_seqs, static_cast<int>(group), s)
-                         : dispatch_group<64>(a, num_seqs, static_cast<int>(group), s);
+  // tiles of 16 cache rows per split of the longest request
+  const int64_t split_tiles = ((max_seq_len + 15) / 16 + pow2 - 1) / pow2;
+  return head_dim == 128
+             ? dispatch_group<128>(a, num_seqs, split_tiles, static_cast<int>(group), device, s)
+             : dispatch_group<64>(a, num_seqs, split_tiles, static_cast<int>(group), device, s);
 }

@@ -52,7 +52,8 @@ def make_case(cuda, seqs, heads, kv_heads, dim, max_len, bs, seed):
     (5, 32, 8, 64, 300, 16),      # Llama-3.2-1B
     (4, 8, 1, 128, 900, 16),      # eight query heads per KV head
     (3, 16, 4, 128, 777, 16),     # four query heads per KV head
-    (2, 4, 4, 64, 5000, 16),      # no grouping, long contexts
+    (2, 4, 4, 64, 5000, 16),      # no grouping, long contexts (16-warp CTAs)
+    (1, 16, 8, 128, 4096, 16),    # one long request: 16-warp CTAs at head dim 128
     (3, 16, 8, 128, 333, 1),      # one row per page
     (3, 16, 8, 128, 1000, 12),    # pages that tiles of 16 rows straddle
     (2, 16, 8, 64, 1500, 3),
