@@ -285,8 +285,9 @@ int svllm_paged_decode_attention_bf16(void* out, const void* q, int64_t q_token_
  * [out_features, in_features] bf16 at weight_stride elements (a checkpoint's projection, no
  * bias); out: [num_rows, out_features] bf16 at out_stride elements. More than 16 rows,
  * in_features not a multiple of 8, or x or weight not 16-byte aligned with strides of whole 16
- * bytes: SVLLM_ERR_UNSUPPORTED, and the caller's GEMM serves the call. Replaces, for decode
- * steps, at::linear in the model forward the reference plans (src/model, docs/ROADMAP.md:24-25).
+ * bytes: SVLLM_ERR_UNSUPPORTED, and the caller's GEMM serves the call. out must not overlap x.
+ * Replaces, for decode steps, at::linear in the model forward the reference plans (src/model,
+ * docs/ROADMAP.md:24-25).
  */
 int svllm_decode_linear_bf16(void* out, int64_t out_stride, const void* x, int64_t num_rows,
                              int64_t in_features, int64_t x_stride, const void* weight,
