@@ -64,9 +64,49 @@ INVALID = 1
     lambda L: L.svllm_rope_inv_freq(-1.0, 8, None, 8),
     lambda L: L.svllm_set_pipeline(b"no_such_op", 0, 0, 0),
     lambda L: L.svllm_set_pipeline(b"rms_norm", 100, 0, 0),
+    # decode linear: in_features 0; out_stride < out_features; null x
+    lambda L: L.svllm_decode_linear_bf16(256, 64, 256, 1, 0, 64, 256, 64, 64, None),
+    lambda L: L.svllm_decode_linear_bf16(256, 32, 256, 1, 64, 64, 256, 64, 64, None),
+    lambda L: L.svllm_decode_linear_bf16(256, 64, None, 1, 64, 64, 256, 64, 64, None),
+    # paged decode attention: 6 heads over 4 KV heads; max_seq_len past the table; null q
+    lambda L: L.svllm_paged_decode_attention_bf16(256, 256, 768, 256, 256, 4, 16, 256, 2, 256,
+                                                  1, 6, 4, 128, 16, 0.1, None),
+    lambda L: L.svllm_paged_decode_attention_bf16(256, 256, 2048, 256, 256, 4, 16, 256, 2, 256,
+                                                  1, 16, 8, 128, 33, 0.1, None),
+    lambda L: L.svllm_paged_decode_attention_bf16(256, None, 2048, 256, 256, 4, 16, 256, 2, 256,
+                                                  1, 16, 8, 128, 32, 0.1, None),
+    # fused LM head + argmax: vocabulary 0; a workspace of 8 bytes for 2 rows
+    lambda L: L.svllm_lm_head_argmax_bf16(256, 2, 64, 64, 256, 0, 64, 256, None, 0, 256, 16, None),
+    lambda L: L.svllm_lm_head_argmax_bf16(256, 2, 64, 64, 256, 100, 64, 256, None, 0, 256, 8,
+                                          None),
+    lambda L: L.svllm_lm_head_argmax_static_bf16(256, 2, 64, 64, 256, 100, 64, 256, 256, 50,
+                                                 None),  # logits_stride < vocab
 ], ids=lambda c: "")
 def test_bad_arguments_are_rejected_without_a_gpu(call):
     assert call(capi.lib()) == INVALID
+
+
+UNSUPPORTED, TOO_LARGE = 3, 2
+
+
+@pytest.mark.parametrize("call, status", [
+    # 17 token rows: more than a decode batch, the caller's GEMM takes it
+    (lambda L: L.svllm_decode_linear_bf16(256, 64, 256, 17, 64, 64, 256, 64, 64, None),
+     UNSUPPORTED),
+    # in_features not a multiple of 8
+    (lambda L: L.svllm_decode_linear_bf16(256, 64, 256, 2, 60, 64, 256, 64, 64, None),
+     UNSUPPORTED),
+    # head_dim 96; three query heads per KV head
+    (lambda L: L.svllm_paged_decode_attention_bf16(256, 256, 1536, 256, 256, 4, 16, 256, 2, 256,
+                                                   1, 16, 8, 96, 32, 0.1, None), UNSUPPORTED),
+    (lambda L: L.svllm_paged_decode_attention_bf16(256, 256, 768, 256, 256, 4, 16, 256, 2, 256,
+                                                   1, 6, 2, 128, 32, 0.1, None), UNSUPPORTED),
+    # the allocation-free LM head takes at most 4096 rows
+    (lambda L: L.svllm_lm_head_argmax_static_bf16(256, 4097, 64, 64, 256, 100, 64, 256, None, 0,
+                                                  None), TOO_LARGE),
+], ids=lambda c: "")
+def test_shapes_without_a_kernel_are_refused_without_a_gpu(call, status):
+    assert call(capi.lib()) == status
 
 
 def test_empty_batches_are_a_no_op_without_a_gpu():
@@ -75,6 +115,12 @@ def test_empty_batches_are_a_no_op_without_a_gpu():
     assert lib.svllm_add_rms_norm_f32(None, None, None, 0, 1024, 1024, 1024, 1e-6, None) == 0
     assert lib.svllm_silu_and_mul_bf16(None, None, None, 0, 3072, 3072, 3072, 3072, None) == 0
     assert lib.svllm_embedding_bf16(None, None, 0, None, 0, 10, 16, 16, 16, None, None) == 0
+    assert lib.svllm_decode_linear_bf16(None, 1024, None, 0, 1024, 1024, None, 1024, 1024,
+                                        None) == 0
+    assert lib.svllm_paged_decode_attention_bf16(None, None, 2048, None, None, 4, 16, None, 2,
+                                                 None, 0, 16, 8, 128, 32, 0.1, None) == 0
+    assert lib.svllm_lm_head_argmax_bf16(None, 0, 64, 64, None, 100, 64, None, None, 0, None, 0,
+                                         None) == 0
     inv = (ctypes.c_float * 64)()
     assert lib.svllm_rope_bf16(None, None, None, 0, 0, 16, 8, 128, 2048, 1024,
                                ctypes.cast(inv, ctypes.c_void_p), None) == 0
