@@ -48,16 +48,6 @@ __device__ __forceinline__ uint4 ld_global_cg_v4(const void* p) {
   return r;
 }
 
-// d += a * b on the tensor cores: A 16x16 bf16 (row), B 16x8 bf16 (col), fp32 accumulators.
-__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                          uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-      "{%8, %9}, {%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
 // NT n-tiles of 8 tokens; W warps per CTA.
 template <int NT, int W>
 __global__ void __launch_bounds__(W * kWarpSize) decode_linear_kernel(const StreamArgs a) {

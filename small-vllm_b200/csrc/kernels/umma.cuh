@@ -1,7 +1,7 @@
-// tcgen05 and TMA building blocks shared by the tensor-core GEMM kernels (the fused LM head +
-// greedy sampling, the decode-sized linear layer): bulk tensor copies into shared memory,
-// TMEM allocation, tcgen05.mma with shared-memory descriptors, commits to mbarriers, TMEM loads,
-// bounded mbarrier waits, and the host-side tensor maps they read through.
+// tcgen05 and TMA building blocks of the tensor-core GEMM (the fused LM head + greedy sampling):
+// bulk tensor copies into shared memory, TMEM allocation, tcgen05.mma with shared-memory
+// descriptors, commits to mbarriers, TMEM loads, bounded mbarrier waits, and the host-side
+// tensor maps they read through.
 #pragma once
 
 #include <cuda.h>
