@@ -286,6 +286,9 @@ int svllm_paged_decode_attention_bf16(void* out, const void* q, int64_t q_token_
  * bias); out: [num_rows, out_features] bf16 at out_stride elements. More than 16 rows,
  * in_features not a multiple of 8, or x or weight not 16-byte aligned with strides of whole 16
  * bytes: SVLLM_ERR_UNSUPPORTED, and the caller's GEMM serves the call. out must not overlap x.
+ * The weight is read before the previous kernel in the stream has finished (programmatic
+ * dependent launch, when that kernel allows it, as this library's kernels do): it must not be
+ * written by the kernel immediately before the call.
  * Replaces, for decode steps, at::linear in the model forward the reference plans (src/model,
  * docs/ROADMAP.md:24-25).
  */
