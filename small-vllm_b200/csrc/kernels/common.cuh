@@ -206,8 +206,8 @@ __device__ __forceinline__ uint4 ld_shared_v4(const void* p) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// mbarrier + bulk copy (cp.async.bulk, the non-tensor TMA path). No .multicast::cluster form is
-// used anywhere in this library: every copy moves this GPU's own memory into its own CTA.
+// mbarrier + bulk copy (cp.async.bulk, the non-tensor TMA path). No copy in this library is
+// broadcast to other CTAs of a cluster: every copy moves this GPU's own memory into its own CTA.
 
 // Programmatic dependent launch: wait until the kernel before this one in the stream has
 // completed and its memory is visible (a no-op when launched without the attribute), then let
