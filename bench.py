@@ -242,6 +242,7 @@ class ClockSampler:
         self.period = period_s
         self.samples: list[tuple[int, float, float, int]] = []
         self._stop = None
+        self._ready = None
         self._thread = None
 
     def _poll(self):
@@ -259,6 +260,7 @@ class ClockSampler:
                     self.samples.append((i, float(sm), float(mx), int(rs)))
                 except pynvml.NVMLError:
                     pass
+            self._ready.set()
             self._stop.wait(self.period)
 
     def __enter__(self):
@@ -273,8 +275,11 @@ class ClockSampler:
         except Exception:  # NVML missing: report no samples rather than fail the bench
             return self
         self._stop = threading.Event()
+        self._ready = threading.Event()
         self._thread = threading.Thread(target=self._poll, daemon=True)
         self._thread.start()
+        # the timed region can be shorter than the thread's NVML set-up: start it once polling runs
+        self._ready.wait(timeout=2.0)
         return self
 
     def __exit__(self, *exc):
