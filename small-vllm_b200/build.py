@@ -63,10 +63,22 @@ def _run(cmd: list[str]) -> None:
                            f"{proc.stdout}\n{proc.stderr}")
 
 
+def kernel_sources() -> list[Path]:
+    """The CUDA sources of libsvllm_kernels.so (CMakeLists.txt globs the same files)."""
+    return sorted((CSRC / "kernels").glob("*.cu"))
+
+
+def op_sources() -> list[Path]:
+    """The C++ sources of the svllm_ops module: the op layer, the model forward and the binding
+    (CMakeLists.txt globs the same files)."""
+    return (sorted((CSRC / "ops").rglob("*.cpp")) + sorted((CSRC / "model").glob("*.cpp")) +
+            sorted((CSRC / "bindings").glob("*.cpp")))
+
+
 def build_kernels(force: bool, jobs: int, verbose_ptxas: bool = False) -> Path:
     """Compiles csrc/kernels/*.cu for sm_100a and links libsvllm_kernels.so."""
     kdir = CSRC / "kernels"
-    sources = sorted(kdir.glob("*.cu"))
+    sources = kernel_sources()
     headers = sorted(kdir.glob("*.cuh")) + sorted(kdir.glob("*.h")) + [INCLUDE / "svllm_kernels.h"]
     obj_dir = BUILD / "kernels"
     obj_dir.mkdir(parents=True, exist_ok=True)
@@ -136,8 +148,7 @@ def build_ops(force: bool, jobs: int) -> Path:
     """Compiles the LibTorch op layer and the pybind11 module svllm_ops."""
     # The system g++ ships OpenMP's spec files; a toolchain on CXX may not.
     cxx = "/usr/bin/g++" if Path("/usr/bin/g++").exists() else os.environ.get("CXX", "g++")
-    sources = (sorted((CSRC / "ops").rglob("*.cpp")) + sorted((CSRC / "model").glob("*.cpp")) +
-               sorted((CSRC / "bindings").glob("*.cpp")))
+    sources = op_sources()
     headers = (sorted((CSRC / "ops").rglob("*.h")) + sorted((CSRC / "model").glob("*.h")) +
                [INCLUDE / "svllm_kernels.h"])
     obj_dir = BUILD / "ops"
