@@ -7,6 +7,13 @@
    from the sources where they lie under the reference checkout, for sm_100a, with the binding
    oracle/ref_binding.cpp. Only built when the reference checkout is present (this container);
    the built file travels with the tree. Outputs go to oracle/_ref/ only.
+3. oracle/_ref/reference_tests/: the reference's own Python tests of the op API, unmodified
+   (tests/python/conftest.py, test_rms_norm.py, test_bindings.py, and the pyproject.toml whose
+   version test_bindings.py checks), copied in the reference's layout so that they run against
+   this build's svllm_ops with SVLLM_BUILD_DIR pointing at it (tests/test_reference_suite.py).
+
+The reference checkout is given by --reference or the SVLLM_REFERENCE environment variable;
+without either, only the restatement is built.
 
 Usage: python oracle/build.py [--force] [--reference PATH]
 """
@@ -23,7 +30,10 @@ from pathlib import Path
 ORACLE = Path(__file__).resolve().parent
 REF_OUT = ORACLE / "_ref"
 ORACLE_LIB = ORACLE / "libsvllm_oracle.so"
-DEFAULT_REFERENCE = Path("/root/reference")
+REF_TESTS = REF_OUT / "reference_tests"
+# The reference's test files run unmodified, in its layout (REPO_ROOT = tests/python/../..).
+REF_TEST_FILES = ["pyproject.toml", "tests/python/conftest.py", "tests/python/test_rms_norm.py",
+                  "tests/python/test_bindings.py"]
 CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 
 
@@ -94,16 +104,40 @@ def build_reference(reference: Path, force: bool = False) -> Path | None:
     return target
 
 
-def build(force: bool = False, reference: Path = DEFAULT_REFERENCE) -> None:
+def stage_reference_tests(reference: Path) -> Path | None:
+    """Copies the reference's op-API tests, byte for byte, into oracle/_ref/reference_tests/."""
+    import shutil
+
+    if not all((reference / f).exists() for f in REF_TEST_FILES):
+        return None
+    for f in REF_TEST_FILES:
+        dst = REF_TESTS / f
+        dst.parent.mkdir(parents=True, exist_ok=True)
+        shutil.copyfile(reference / f, dst)
+    return REF_TESTS
+
+
+def reference_dir(explicit: Path | None = None) -> Path | None:
+    """The reference checkout: the explicit path, else $SVLLM_REFERENCE, else None."""
+    if explicit is not None:
+        return explicit
+    env = os.environ.get("SVLLM_REFERENCE")
+    return Path(env) if env else None
+
+
+def build(force: bool = False, reference: Path | None = None) -> None:
     build_oracle(force)
-    if reference.exists():
+    reference = reference_dir(reference)
+    if reference is not None and reference.exists():
         build_reference(reference, force)
+        stage_reference_tests(reference)
 
 
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--force", action="store_true")
-    parser.add_argument("--reference", type=Path, default=DEFAULT_REFERENCE)
+    parser.add_argument("--reference", type=Path, default=None,
+                        help="the reference checkout (default: $SVLLM_REFERENCE)")
     args = parser.parse_args()
     build(args.force, args.reference)
     return 0
