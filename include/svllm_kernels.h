@@ -318,14 +318,6 @@ int svllm_lm_head_argmax_static_bf16(const void* hidden, int64_t num_rows, int64
  */
 int svllm_read_device_error(int device, int reset, int* flags);
 
-/*
- * Tuning knob for the bulk-copy pipelines of one op ("rms_norm", "add_rms_norm", "qk_norm_rope",
- * "rope", "silu_and_mul", "embedding"): target bytes per pipeline stage, stages per warp and
- * warps per CTA; 0 keeps the current value. Results do not depend on it. Not thread-safe
- * against concurrent launches of the same op.
- */
-int svllm_set_pipeline(const char* op, int64_t unit_bytes, int64_t stages, int64_t warps);
-
 #ifdef __cplusplus
 }
 #endif

@@ -337,6 +337,39 @@ __device__ __forceinline__ void bulk_store(void* dst_gmem, const void* src_smem,
                : "memory");
 }
 
+// L2 cache policies for the bulk copies' cache hints: evict-last for data the kernel will read
+// again soon (kept in L2 ahead of normal lines), evict-first for data it writes once.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// bulk_load with an L2 cache policy.
+__device__ __forceinline__ void bulk_load_policy(void* dst_smem, const void* src_gmem,
+                                                 uint32_t bytes, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+      "[%1], %2, [%3], %4;" ::"r"(smem_addr(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+// bulk_store with an L2 cache policy.
+__device__ __forceinline__ void bulk_store_policy(void* dst_gmem, const void* src_smem,
+                                                  uint32_t bytes, uint64_t policy) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group.L2::cache_hint [%0], [%1], %2, %3;" ::
+                   "l"(dst_gmem),
+               "r"(smem_addr(src_smem)), "r"(bytes), "l"(policy)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }

@@ -10,6 +10,14 @@
 //     output row with a bulk shared->global store, refilling a stage once the store that read it
 //     has drained. The warp's 32 lanes fetch ids 32 at a time (coalesced, one batch ahead) and
 //     hand them to lane 0 by shuffle.
+//   * Vocabulary buckets: when the batch reads table rows more than once on average, the warp
+//     walks its tokens in `passes` rounds and round p copies only the tokens whose id lies in
+//     the p-th slice of the vocabulary. The whole grid then reads from one L2-sized slice of the
+//     table at a time, so repeated rows come from L2 instead of HBM (at 1M tokens over a
+//     151,936-row table each row is read ~6.9 times). Output rows are written where they belong,
+//     so the result does not depend on the order. Table loads carry an L2 evict-last policy and
+//     the output stores an evict-first one, so the stream of output rows does not push the slice
+//     out of L2.
 //   * An id outside [0, vocab) zeroes its row and raises SVLLM_DEVERR_BAD_INDEX; nothing faults.
 //   * Plain path for unaligned or odd-sized rows: one warp per row, element copies.
 #include <cuda_runtime.h>
@@ -38,7 +46,9 @@ struct EmbArgs {
   // bulk-copy path
   int stages;
   int stage_bytes;
-  int ring_offset;
+  int ring_offset;       // after the mbarriers and the per-stage token slots
+  int passes;            // vocabulary buckets, one per pass over the warp's tokens
+  int64_t bucket_rows;   // rows per bucket: ceil(vocab / passes)
 };
 
 __device__ __forceinline__ int64_t load_id(const void* ids, int is_i64, int64_t t) {
@@ -53,7 +63,11 @@ __global__ void __launch_bounds__(512) embedding_bulk_kernel(const EmbArgs a) {
   const int warp = threadIdx.x / kWarpSize;
   const int lane = threadIdx.x % kWarpSize;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * a.stages;
+  // the output row each stage holds (-1: nothing to store), written and read by lane 0 only
+  int64_t* stage_token = reinterpret_cast<int64_t*>(smem) + (warps + warp) * a.stages;
   uint8_t* ring = smem + a.ring_offset + static_cast<size_t>(warp) * a.stages * a.stage_bytes;
+  const uint64_t load_policy = l2_policy_evict_last();
+  const uint64_t store_policy = l2_policy_evict_first();
 
   if (lane == 0) {
     for (int s = 0; s < a.stages; ++s) mbar_init(&bars[s], 1);
@@ -67,30 +81,65 @@ __global__ void __launch_bounds__(512) embedding_bulk_kernel(const EmbArgs a) {
   const int64_t n = t1 - t0;
   if (n <= 0) return;
 
-  // ids of rows [base, base + 32) in `cur`, the next 32 in `nxt` (one lane each).
-  auto load_batch = [&](int64_t base) -> int64_t {
-    return base + lane < n ? load_id(a.ids, a.ids_i64, t0 + base + lane) : 0;
+  // The warp's tokens in pass order: pass p visits the tokens t0.. t1-1 whose id is in bucket p
+  // (an id outside the table belongs to pass 0). `chunk` holds this lane's id in the current
+  // 32-token chunk, `next_chunk` the chunk after it, `pending` the lanes of the current chunk
+  // still to be visited in this pass.
+  auto load_chunk = [&](int64_t base) -> int64_t {
+    return base + lane < n ? load_id(a.ids, a.ids_i64, t0 + base + lane) : -1;
   };
-  int64_t cur_base = 0;
-  int64_t cur = load_batch(0);
-  int64_t nxt = load_batch(kWarpSize);
+  auto in_pass = [&](int64_t id, int pass) -> bool {
+    const bool valid = id >= 0 && id < a.vocab;
+    return (valid ? static_cast<int>(id / a.bucket_rows) : 0) == pass;
+  };
+  int pass = 0;
+  int64_t base = 0;
+  int64_t chunk = load_chunk(0);
+  int64_t next_chunk = load_chunk(n > kWarpSize ? kWarpSize : 0);
+  uint32_t pending = __ballot_sync(0xffffffffu, base + lane < n && in_pass(chunk, 0));
 
-  // Warp-collective: fills stage s with the table row of token index i (i increasing).
-  auto refill = [&](int64_t i, int s) {
-    while (i >= cur_base + kWarpSize) {
-      cur = nxt;
-      cur_base += kWarpSize;
-      nxt = load_batch(cur_base + kWarpSize);
+  // Warp-collective: the next (token, id) in pass order; token -1 once every pass is done
+  // (never reached when called at most n times, since every token is in exactly one pass).
+  auto next = [&](int64_t& token, int64_t& id) {
+    while (pending == 0) {
+      if (pass >= a.passes) {
+        token = -1;
+        id = 0;
+        return;
+      }
+      base += kWarpSize;
+      if (base >= n) {
+        base = 0;
+        ++pass;
+      }
+      chunk = next_chunk;
+      const int64_t after = base + kWarpSize < n ? base + kWarpSize : 0;
+      next_chunk = load_chunk(after);
+      pending = __ballot_sync(0xffffffffu, base + lane < n && in_pass(chunk, pass));
     }
-    const int64_t id = __shfl_sync(0xffffffffu, cur, static_cast<int>(i - cur_base));
+    const int l = __ffs(pending) - 1;
+    pending &= pending - 1;
+    id = __shfl_sync(0xffffffffu, chunk, l);
+    token = t0 + base + l;
+  };
+
+  // Warp-collective: fills stage s with the next token's table row.
+  auto refill = [&](int s) {
+    int64_t token, id;
+    next(token, id);
     uint8_t* st = ring + static_cast<size_t>(s) * a.stage_bytes;
     // The stage's previous row must have been read out by its bulk store before it is reused.
-    if (lane == 0) bulk_wait_read<1>();
-    if (id >= 0 && id < a.vocab) {
+    if (lane == 0) {
+      bulk_wait_read<1>();
+      stage_token[s] = token;
+    }
+    if (token < 0) {
+      if (lane == 0) mbar_arrive(&bars[s]);
+    } else if (id >= 0 && id < a.vocab) {
       if (lane == 0) {
         mbar_arrive_expect_tx(&bars[s], a.row_bytes);
-        bulk_load(st, static_cast<const uint8_t*>(a.table) + id * a.table_stride_bytes,
-                  a.row_bytes, &bars[s]);
+        bulk_load_policy(st, static_cast<const uint8_t*>(a.table) + id * a.table_stride_bytes,
+                         a.row_bytes, &bars[s], load_policy);
       }
     } else {
       __syncwarp();
@@ -107,7 +156,7 @@ __global__ void __launch_bounds__(512) embedding_bulk_kernel(const EmbArgs a) {
   };
 
   for (int64_t j = 0; j < min(static_cast<int64_t>(a.stages), n); ++j) {
-    refill(j, static_cast<int>(j));
+    refill(static_cast<int>(j));
   }
 
   int64_t j = 0;
@@ -115,14 +164,15 @@ __global__ void __launch_bounds__(512) embedding_bulk_kernel(const EmbArgs a) {
     const int s = static_cast<int>(j % a.stages);
     const uint32_t parity = static_cast<uint32_t>((j / a.stages) & 1);
     if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[s], parity))) break;
-    if (lane == 0) {
-      bulk_store(static_cast<uint8_t*>(a.out) + (t0 + j) * a.out_stride_bytes,
-                 ring + static_cast<size_t>(s) * a.stage_bytes, a.row_bytes);
+    if (lane == 0 && stage_token[s] >= 0) {
+      bulk_store_policy(static_cast<uint8_t*>(a.out) + stage_token[s] * a.out_stride_bytes,
+                        ring + static_cast<size_t>(s) * a.stage_bytes, a.row_bytes,
+                        store_policy);
       bulk_commit();
     }
     // Refill the stage of the previous row, whose store has had a row's time to drain.
     if (j >= 1 && j - 1 + a.stages < n) {
-      refill(j - 1 + a.stages, static_cast<int>((j - 1) % a.stages));
+      refill(static_cast<int>((j - 1) % a.stages));
     }
   }
 
@@ -195,17 +245,31 @@ int launch_embedding(void* out, const void* ids, int id_type, const void* table,
   if (bulk_ok) {
     const PipelineShape shape = pipeline_shape(OpId::kEmbedding);
     a.stage_bytes = static_cast<int>(round_up(a.row_bytes, 128));
+    // Vocabulary buckets of about kBucketBytes of table each (measured on a B200 at 1M tokens
+    // of 2 KB rows over a 151,936-row table: 8 buckets 7.8, 16 8.5, 24 9.9, 32 9.4 TB/s of
+    // algorithmic bytes). Below one read per table row on average there is little reuse to
+    // gain and the gather walks its tokens once.
+    constexpr int64_t kBucketBytes = 13ll << 20;
+    constexpr int kMaxPasses = 64;
+    const int64_t table_bytes = vocab * static_cast<int64_t>(a.row_bytes);
+    a.passes = num_tokens >= vocab
+                   ? static_cast<int>(std::min<int64_t>(
+                         kMaxPasses, std::max<int64_t>(1, (table_bytes + kBucketBytes - 1) /
+                                                              kBucketBytes)))
+                   : 1;
+    a.bucket_rows = (vocab + a.passes - 1) / a.passes;
     int warps = warps_for(num_tokens, shape.warps, device);
     int stages = shape.stages;
+    // per stage: an mbarrier and the token slot (8 bytes each), then the row
     auto smem_for = [&](int w, int s) {
-      return round_up(static_cast<int64_t>(w) * s * 8, 128) +
+      return round_up(static_cast<int64_t>(w) * s * 16, 128) +
              static_cast<int64_t>(w) * s * a.stage_bytes;
     };
     while (smem_for(warps, stages) > static_cast<int64_t>(kMaxSmemPerCta) && stages > 2) --stages;
     while (smem_for(warps, stages) > static_cast<int64_t>(kMaxSmemPerCta) && warps > 1) --warps;
     if (smem_for(warps, stages) <= static_cast<int64_t>(kMaxSmemPerCta)) {
       a.stages = stages;
-      a.ring_offset = static_cast<int>(round_up(static_cast<int64_t>(warps) * stages * 8, 128));
+      a.ring_offset = static_cast<int>(round_up(static_cast<int64_t>(warps) * stages * 16, 128));
       const size_t smem = static_cast<size_t>(smem_for(warps, stages));
       const int threads = warps * kWarpSize;
       const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(embedding_bulk_kernel),

@@ -1,9 +1,13 @@
 // Host-side launch plumbing and the small C-ABI entry points that launch no kernel.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <string>
 #include <unordered_map>
 
 #include "host_common.h"
@@ -25,13 +29,13 @@ std::atomic<int*> g_error_word[kMaxDevices];
 // resident warps of loads in flight per SM well above the ~45 KB that 6.5 TB/s over 148 SMs
 // needs at ~1 us of memory latency; the compute-heavier ops (SiLU, q/k norm + RoPE) also want
 // many resident warps to hide their latency chains.
-PipelineShape g_shapes[static_cast<int>(OpId::kCount)] = {
+constexpr PipelineShape kDefaultShapes[static_cast<int>(OpId::kCount)] = {
     {8192, 2, 8},   // rms_norm
     {4096, 4, 8},   // add_rms_norm
     {4096, 2, 16},  // qk_norm_rope (a unit is one token; unit_bytes is unused)
-    {4096, 2, 16},  // rope
+    {4096, 3, 10},  // rope
     {8192, 2, 6},   // silu_and_mul (the table path leaves ~99 KB of shared memory for stages)
-    {4096, 3, 4},   // embedding (a unit is one row; unit_bytes is unused)
+    {4096, 6, 8},   // embedding (a unit is one row; unit_bytes is unused)
 };
 
 const char* const kOpNames[] = {"rms_norm", "add_rms_norm", "qk_norm_rope",
@@ -62,25 +66,47 @@ std::mutex g_occ_mutex;
 std::unordered_map<OccKey, int, OccKeyHash> g_occ;
 std::unordered_map<OccKey, bool, OccKeyHash> g_attr;  // keyed by (func, device) only
 
+// The shapes in force: the defaults, with the overrides of the SVLLM_PIPELINE environment
+// variable applied once, on first use, and never changed afterwards (so the C ABI has no mutable
+// launch state). The variable is a tuning and test hook: "op=unit_bytes:stages:warps[,op=...]",
+// 0 keeping a default; entries that do not parse or are out of range are ignored. Results do not
+// depend on the shape.
+const PipelineShape* shapes_in_force() {
+  static PipelineShape shapes[static_cast<int>(OpId::kCount)];
+  static std::once_flag once;
+  std::call_once(once, [] {
+    std::memcpy(shapes, kDefaultShapes, sizeof(shapes));
+    const char* env = std::getenv("SVLLM_PIPELINE");
+    if (env == nullptr) return;
+    const std::string spec(env);
+    size_t pos = 0;
+    while (pos <= spec.size()) {
+      const size_t end = std::min(spec.find(',', pos), spec.size());
+      const std::string item = spec.substr(pos, end - pos);
+      pos = end + 1;
+      const size_t eq = item.find('=');
+      if (eq == std::string::npos) continue;
+      long long unit = -1, stages = -1, warps = -1;
+      if (std::sscanf(item.c_str() + eq + 1, "%lld:%lld:%lld", &unit, &stages, &warps) != 3 ||
+          unit < 0 || stages < 0 || warps < 0 || unit > (1 << 20) || unit % 16 != 0 ||
+          stages > 16 || warps > 32 || (stages != 0 && stages < 2)) {
+        continue;
+      }
+      for (int i = 0; i < static_cast<int>(OpId::kCount); ++i) {
+        if (item.compare(0, eq, kOpNames[i]) == 0 && std::strlen(kOpNames[i]) == eq) {
+          if (unit) shapes[i].unit_bytes = static_cast<int>(unit);
+          if (stages) shapes[i].stages = static_cast<int>(stages);
+          if (warps) shapes[i].warps = static_cast<int>(warps);
+        }
+      }
+    }
+  });
+  return shapes;
+}
+
 }  // namespace
 
-PipelineShape pipeline_shape(OpId op) { return g_shapes[static_cast<int>(op)]; }
-
-int set_pipeline_shape(const char* op, int64_t unit_bytes, int64_t stages, int64_t warps) {
-  if (op == nullptr || unit_bytes < 0 || stages < 0 || warps < 0 || unit_bytes > (1 << 20) ||
-      stages > 16 || warps > 32 || (unit_bytes % 16) != 0) {
-    return SVLLM_ERR_INVALID_ARGUMENT;
-  }
-  for (int i = 0; i < static_cast<int>(OpId::kCount); ++i) {
-    if (std::strcmp(op, kOpNames[i]) == 0) {
-      if (unit_bytes) g_shapes[i].unit_bytes = static_cast<int>(unit_bytes);
-      if (stages) g_shapes[i].stages = static_cast<int>(stages);
-      if (warps) g_shapes[i].warps = static_cast<int>(warps);
-      return SVLLM_OK;
-    }
-  }
-  return SVLLM_ERR_INVALID_ARGUMENT;
-}
+PipelineShape pipeline_shape(OpId op) { return shapes_in_force()[static_cast<int>(op)]; }
 
 int current_device(int* device) {
   return cudaGetDevice(device) == cudaSuccess && *device >= 0 && *device < kMaxDevices
@@ -193,10 +219,6 @@ int svllm_read_device_error(int device, int reset, int* flags) {
   if (status != SVLLM_OK) cudaGetLastError();
   cudaSetDevice(prev);
   return status;
-}
-
-int svllm_set_pipeline(const char* op, int64_t unit_bytes, int64_t stages, int64_t warps) {
-  return set_pipeline_shape(op, unit_bytes, stages, warps);
 }
 
 }  // extern "C"

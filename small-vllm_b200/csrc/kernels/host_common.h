@@ -21,8 +21,9 @@ struct PipelineShape {
 
 enum class OpId { kRmsNorm, kAddRmsNorm, kQkNormRope, kRope, kSiluAndMul, kEmbedding, kCount };
 
+// The pipeline shape of one op: the library's tuned default, or the override that the
+// SVLLM_PIPELINE environment variable gave when the process first launched a kernel.
 PipelineShape pipeline_shape(OpId op);
-int set_pipeline_shape(const char* op, int64_t unit_bytes, int64_t stages, int64_t warps);
 
 // Devices the per-device caches hold (current_device rejects higher ordinals).
 constexpr int kMaxDevices = 64;

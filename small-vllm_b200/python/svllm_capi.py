@@ -71,7 +71,6 @@ SIGNATURES = {
                                           _I64, _I64, _I64, _I64, ctypes.c_float, _P],
     "svllm_decode_linear_bf16": [_P, _I64, _P, _I64, _I64, _I64, _P, _I64, _I64, _P],
     "svllm_read_device_error": [_I, _I, _P],
-    "svllm_set_pipeline": [ctypes.c_char_p, _I64, _I64, _I64],
 }
 
 _lib: ctypes.CDLL | None = None
@@ -273,9 +272,6 @@ def read_device_error(device: int = 0, reset: bool = True) -> int:
           "read_device_error")
     return flags.value
 
-
-def set_pipeline(op: str, unit_bytes: int = 0, stages: int = 0, warps: int = 0) -> None:
-    check(lib().svllm_set_pipeline(op.encode(), unit_bytes, stages, warps), "set_pipeline")
 
 
 def version() -> str:

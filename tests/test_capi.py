@@ -62,8 +62,6 @@ INVALID = 1
     lambda L: L.svllm_embedding_bf16(8, 8, 0, 8, 4, 0, 16, 16, 16, None, None),   # vocab 0
     lambda L: L.svllm_rope_inv_freq(1e6, 7, None, 8),
     lambda L: L.svllm_rope_inv_freq(-1.0, 8, None, 8),
-    lambda L: L.svllm_set_pipeline(b"no_such_op", 0, 0, 0),
-    lambda L: L.svllm_set_pipeline(b"rms_norm", 100, 0, 0),
     # decode linear: in_features 0; out_stride < out_features; null x
     lambda L: L.svllm_decode_linear_bf16(256, 64, 256, 1, 0, 64, 256, 64, 64, None),
     lambda L: L.svllm_decode_linear_bf16(256, 32, 256, 1, 64, 64, 256, 64, 64, None),

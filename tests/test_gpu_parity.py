@@ -294,6 +294,44 @@ def test_embedding_bad_ids_zero_rows_and_raise_the_error_word(cuda):
     assert capi.read_device_error(0, reset=True) & capi.DEVERR_BAD_INDEX
 
 
+# Batches with at least one token per table row take the vocabulary-bucket walk (the gather
+# visits its tokens once per L2-sized slice of the table); these tables span 2 to 24 slices.
+@pytest.mark.parametrize("vocab, hidden, T, dt, ids_dtype", [
+    (8192, 1024, 16384, torch.bfloat16, torch.int32),
+    (20000, 2048, 40000, torch.bfloat16, torch.int64),
+    (4096, 1024, 9000, torch.float32, torch.int32),
+    (151936, 1024, 300000, torch.bfloat16, torch.int32),
+], ids=str)
+def test_embedding_vocabulary_buckets(cuda, vocab, hidden, T, dt, ids_dtype):
+    table = random_t(vocab, hidden, dtype=dt, device=cuda, seed=24, scale=0.02)
+    g = torch.Generator().manual_seed(25)
+    ids = torch.randint(0, vocab, (T,), generator=g).to(device=cuda, dtype=ids_dtype)
+    out = torch.empty(T, hidden, dtype=dt, device=cuda)
+    capi.embedding(out, ids, table)
+    assert torch.equal(out, table[ids.long()])
+    assert capi.read_device_error(0, reset=True) == 0
+
+
+def test_embedding_vocabulary_buckets_bad_ids_and_strided_rows(cuda):
+    vocab, hidden, T = 8192, 1024, 20000
+    table = random_t(vocab, hidden, device=cuda, seed=26)
+    g = torch.Generator().manual_seed(27)
+    ids = torch.randint(0, vocab, (T,), generator=g)
+    bad = torch.randperm(T, generator=g)[:50]
+    ids[bad] = torch.tensor([-1, vocab, vocab + 7, -(2 ** 40), 2 ** 40]).repeat(10)
+    ids = ids.to(cuda)
+    big = torch.full((T, hidden + 64), 3.0, dtype=torch.bfloat16, device=cuda)
+    out = big[:, 64:]
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    capi.embedding(out, ids, table, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == capi.DEVERR_BAD_INDEX
+    good = (ids >= 0) & (ids < vocab)
+    assert torch.equal(out[good], table[ids[good]])
+    assert not out[~good].any()
+    assert bool((big[:, :64] == 3.0).all())
+
+
 def test_embedding_strided_output_rows(cuda):
     vocab, hidden, T = 5000, 1024, 300
     table = random_t(vocab, hidden, device=cuda, seed=23)
@@ -308,31 +346,61 @@ def test_embedding_strided_output_rows(cuda):
 # ---------------------------------------------------------------------------------------------
 # pipeline shapes do not change results
 
-# the library's built-in shapes (host_common.cu), restored after each override
-DEFAULT_SHAPES = {"rms_norm": (8192, 2, 8), "silu_and_mul": (8192, 2, 6)}
+# The pipeline shape comes from the library's defaults, or from the SVLLM_PIPELINE environment
+# variable read once per process; each override runs in a fresh interpreter.
+PIPELINE_PROBE = r"""
+import hashlib, sys
+sys.path[:0] = sys.argv[1:]
+import torch
+import svllm_capi as capi
+from conftest import random_t
+cuda = torch.device("cuda", 0)
+x = random_t(12000, 1024, device=cuda, seed=24)  # enough rows for the bulk-copy kernel
+w = random_t(1024, device=cuda, seed=25)
+gate = random_t(2000, 3072, device=cuda, seed=26)  # chunks of the tuned size, not shrunk
+up = random_t(2000, 3072, device=cuda, seed=27)
+q = random_t(5000, 16, 128, device=cuda, seed=28)
+k = random_t(5000, 8, 128, device=cuda, seed=29)
+pos = torch.arange(5000, device=cuda) * 7
+inv = torch.tensor([1e6 ** (-2 * i / 128) for i in range(64)], dtype=torch.float32)
+table = random_t(4000, 1024, device=cuda, seed=30)
+ids = torch.randint(0, 4000, (9000,), generator=torch.Generator().manual_seed(31)).to(cuda)
+out, sout, eout = torch.empty_like(x), torch.empty_like(gate), torch.empty(9000, 1024, dtype=torch.bfloat16, device=cuda)
+capi.rms_norm(out, x, w, 1e-6)
+capi.silu_and_mul(sout, gate, up)
+capi.rope(q, k, pos, inv)
+capi.embedding(eout, ids, table)
+torch.cuda.synchronize()
+h = hashlib.sha256()
+for t in (out, sout, q, k, eout):
+    h.update(t.view(torch.int16).cpu().numpy().tobytes())
+print(h.hexdigest())
+"""
+
+
+def pipeline_digest(spec: str | None) -> str:
+    import os
+    import subprocess
+    import sys
+
+    from conftest import ORACLE_DIR, PKG_PY, REPO_ROOT
+
+    env = dict(os.environ)
+    env.pop("SVLLM_PIPELINE", None)
+    if spec is not None:
+        env["SVLLM_PIPELINE"] = spec
+    proc = subprocess.run([sys.executable, "-c", PIPELINE_PROBE, str(REPO_ROOT / "tests"),
+                           str(PKG_PY), str(ORACLE_DIR)], capture_output=True, text=True,
+                          env=env, timeout=600)
+    assert proc.returncode == 0, proc.stderr[-3000:]
+    return proc.stdout.strip().splitlines()[-1]
 
 
 @pytest.mark.parametrize("unit, stages, warps", [(2048, 2, 1), (4096, 3, 8), (16384, 4, 2)])
 def test_pipeline_shape_does_not_change_results(cuda, unit, stages, warps):
-    x = random_t(12000, 1024, device=cuda, seed=24)  # enough rows for the bulk-copy kernel
-    w = random_t(1024, device=cuda, seed=25)
-    base = torch.empty_like(x)
-    capi.rms_norm(base, x, w, 1e-6)
-    gate = random_t(2000, 3072, device=cuda, seed=26)  # chunks of the tuned size, not shrunk
-    up = random_t(2000, 3072, device=cuda, seed=27)
-    sbase = torch.empty_like(gate)
-    capi.silu_and_mul(sbase, gate, up)
-    try:
-        for op in ("rms_norm", "silu_and_mul"):
-            capi.set_pipeline(op, unit, stages, warps)
-        out = torch.empty_like(x)
-        capi.rms_norm(out, x, w, 1e-6)
-        sout = torch.empty_like(gate)
-        capi.silu_and_mul(sout, gate, up)
-    finally:
-        for op, shape in DEFAULT_SHAPES.items():
-            capi.set_pipeline(op, *shape)
-    assert torch.equal(out, base) and torch.equal(sout, sbase)
+    spec = ",".join(f"{op}={unit}:{stages}:{warps}"
+                    for op in ("rms_norm", "silu_and_mul", "rope", "embedding"))
+    assert pipeline_digest(spec) == pipeline_digest(None)
 
 
 def test_silu_table_path_is_exhaustively_identical(cuda):
