@@ -53,6 +53,7 @@ def lib() -> ctypes.CDLL:
             "orc_silu_and_mul_bf16": [_P, _P, _P, _I64, _I64],
             "orc_silu_and_mul_f32": [_P, _P, _P, _I64, _I64],
             "orc_embedding": [_P, _P, _I, _P, _I64, _I64, _I64],
+            "orc_set_num_threads": [_I],
         }
         for name, args in sigs.items():
             fn = getattr(_lib, name)
@@ -156,10 +157,12 @@ def inv_freq(theta: float, head_dim: int, scaling: tuple | None = None) -> np.nd
     return out
 
 
-def silu_and_mul(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+def silu_and_mul(gate: np.ndarray, up: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+    """Returns silu(gate) * up, written into `out` when given (contiguous, gate's shape)."""
     dt = gate.dtype
     g, u = _c(gate, dt), _c(up, dt)
-    out = np.empty_like(g)
+    if out is None:
+        out = np.empty_like(g)
     inter = g.shape[-1]
     rows = g.size // inter if inter else 0
     fn = lib().orc_silu_and_mul_bf16 if _is_bf16(gate) else lib().orc_silu_and_mul_f32
@@ -167,17 +170,24 @@ def silu_and_mul(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
     return out
 
 
-def embedding(ids: np.ndarray, table: np.ndarray) -> tuple[np.ndarray, int]:
-    """Returns (rows, number of ids outside [0, vocab))."""
+def embedding(ids: np.ndarray, table: np.ndarray,
+              out: np.ndarray | None = None) -> tuple[np.ndarray, int]:
+    """Returns (rows, number of ids outside [0, vocab)); rows go into `out` when given."""
     ids_c = np.ascontiguousarray(ids)
     is64 = 1 if ids_c.dtype == np.int64 else 0
     if not is64:
         ids_c = _c(ids_c, np.int32)
     tab = np.ascontiguousarray(table)
-    out = np.empty(ids_c.shape + (tab.shape[1],), dtype=tab.dtype)
+    if out is None:
+        out = np.empty(ids_c.shape + (tab.shape[1],), dtype=tab.dtype)
     bad = lib().orc_embedding(_ptr(out), _ptr(ids_c), is64, _ptr(tab), ids_c.size, tab.shape[0],
                               tab.shape[1] * tab.itemsize)
     return out, int(bad)
+
+
+def set_num_threads(n: int) -> int:
+    """Threads of the oracle's OpenMP loops; returns the count in force."""
+    return int(lib().orc_set_num_threads(int(n)))
 
 
 # ---------------------------------------------------------------------------------------------

@@ -31,6 +31,7 @@
  * (tests/golden/make_golden.py writes the fixtures, tests/test_oracle_golden.py checks them).
  */
 #include <math.h>
+#include <omp.h>
 #include <stdint.h>
 #include <string.h>
 
@@ -323,4 +324,11 @@ EXPORT int64_t orc_embedding(void* out, const void* ids, int ids_i64, const void
     }
   }
   return bad;
+}
+
+/* Threads of the OpenMP loops above (the CPU baseline sets it to the cores it reports, whatever
+   OMP_NUM_THREADS the launcher exported). Returns the count now in force. */
+EXPORT int orc_set_num_threads(int n) {
+  if (n > 0) omp_set_num_threads(n);
+  return omp_get_max_threads();
 }
