@@ -45,29 +45,69 @@ LLAMA = dict(name="llama-3.2-1b", hidden=2048, heads=32, kv_heads=8, head_dim=64
 #   add_rms_norm  read x and residual, write residual' and the normed x
 #   qk_norm_rope  read and write q (16 x 128) and k (8 x 128) in place, plus the position
 #   silu_and_mul  read gate and up, write out
-def op_bytes(cfg: dict) -> dict[str, int]:
+def op_bytes(cfg: dict, elem: int = 2) -> dict[str, int]:
+    """Bytes per token of each op, activations of `elem` bytes (2: bf16, 4: fp32)."""
     h, hd, inter = cfg["hidden"], cfg["head_dim"], cfg["inter"]
     heads = cfg["heads"] + cfg["kv_heads"]
-    kv_row = cfg["kv_heads"] * hd * 2
-    rotary = 2 * heads * hd * 2 + 8
+    kv_row = cfg["kv_heads"] * hd * elem
+    rotary = 2 * heads * hd * elem + 8
     if cfg.get("kv_cache"):
         rotary += kv_row + 2 * kv_row + 8  # k into the cache; v read and written; the slot
     return {
-        "embedding": 2 * h * 2 + 4,
-        "add_rms_norm": 4 * h * 2,
+        "embedding": 2 * h * elem + 4,
+        "add_rms_norm": 4 * h * elem,
         rotary_op(cfg): rotary,
-        "silu_and_mul": 3 * inter * 2,
+        "silu_and_mul": 3 * inter * elem,
     }
 
 
 OPS = ["embedding", "add_rms_norm", "qk_norm_rope", "silu_and_mul"]
 WORKLOADS = {
-    # name: (model, total tokens, positions: ("uniform", hi) or ("packed", sequence length))
+    # name: (model, total tokens, positions): positions ("uniform", hi) draw each token's
+    # position from [0, hi); ("packed", n) are sequences of n tokens at positions 0..n-1;
+    # ("sequences", count, lo, hi) are `count` sequences of seeded lengths in [lo, hi], packed,
+    # each at positions 0..len-1 (the total is their summed length)
     "sweep": (QWEN3, 1_048_576, ("uniform", 32768)),
-    "prefill": (QWEN3, 70_000, ("uniform", 2048)),
+    "prefill": (QWEN3, None, ("sequences", 64, 128, 2048)),
     "decode": (QWEN3, 256, ("uniform", 4096)),
     "llama": (LLAMA, 16_384, ("packed", 2048)),
 }
+
+
+def sequence_lengths(pos_spec: tuple):
+    """The seeded sequence lengths of a ("sequences", count, lo, hi) workload."""
+    import numpy as np
+
+    _, count, lo, hi = pos_spec
+    return np.random.default_rng(2025).integers(lo, hi + 1, count)
+
+
+def workload_total(name: str, override: int = 0) -> int:
+    cfg, total, pos_spec = WORKLOADS[name]
+    if override:
+        return override
+    return int(sequence_lengths(pos_spec).sum()) if total is None else total
+
+
+def global_positions(pos_spec: tuple, total: int):
+    """Positions of every token of a "packed" or "sequences" workload (numpy int64)."""
+    import numpy as np
+
+    if pos_spec[0] == "packed":
+        return np.arange(total, dtype=np.int64) % pos_spec[1]
+    lengths = sequence_lengths(pos_spec)
+    pos = np.concatenate([np.arange(n, dtype=np.int64) for n in lengths])
+    reps = -(-total // pos.size)  # a --tokens override beyond the sequences repeats them
+    return np.tile(pos, reps)[:total]
+
+
+def positions_label(pos_spec: tuple) -> str:
+    if pos_spec[0] == "uniform":
+        return f"uniform [0, {pos_spec[1]})"
+    if pos_spec[0] == "packed":
+        return f"sequences of {pos_spec[1]}, positions 0..{pos_spec[1] - 1}"
+    return (f"{pos_spec[1]} sequences of seeded lengths in [{pos_spec[2]}, {pos_spec[3]}], "
+            "packed, each at positions 0..len-1")
 
 
 def rotary_op(cfg: dict) -> str:
@@ -89,7 +129,7 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload",
                    choices=sorted(WORKLOADS) + ["sampling", "lm-head", "model-decode",
-                                                "decode-attention", "decode-linear"],
+                                                "decode-attention", "decode-linear", "rms-norm"],
                    default="sweep",
                    help="sampling: greedy argmax over [tokens, 151936] bf16 logits (one op, "
                         "not the chain); lm-head: the tied LM head fused with greedy sampling "
@@ -98,7 +138,9 @@ def parse_args():
                         "decode-attention: the paged decode-attention kernel of one Qwen3-0.6B "
                         "layer beside the gather + SDPA composite it replaces; decode-linear: "
                         "the Qwen3-0.6B projections at decode batch sizes, the decode-linear "
-                        "kernel beside torch.matmul (cuBLAS)")
+                        "kernel beside torch.matmul (cuBLAS); rms-norm: svllm_ops.rms_norm, or "
+                        "with --impl reference the reference's own CUDA rms_norm, at "
+                        "1M x 1024, 16384 x 2048 and 16M x 128")
     p.add_argument("--batches", default="1,8,64,256",
                    help="model-decode: comma-separated decode batch sizes")
     p.add_argument("--context", type=int, default=512,
@@ -107,7 +149,14 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true", help="skip the host-buffer measurement")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-validate", action="store_true")
-    p.add_argument("--cpu-sample-tokens", type=int, default=32768)
+    p.add_argument("--no-configs", action="store_true",
+                   help="skip the benchmark definition's configs 0-3 (measured at N=1 beside "
+                        "the sweep)")
+    p.add_argument("--cpu-sample-tokens", type=int, default=32768,
+                   help="token rows of the cpu_baseline sample in the GPU arm's line")
+    p.add_argument("--reference-tokens", type=int, default=0,
+                   help="--impl reference: token rows per timed pass (default: the workload's "
+                        "full count, the GPU arm's configuration)")
     p.add_argument("--kv-cache", action="store_true",
                    help="the rotary step also writes k and v into a paged KV cache "
                         "(qk_norm_rope_cache / rope_cache)")
@@ -158,7 +207,7 @@ def make_inputs(T: int, pos_spec: tuple, cfg: dict, device, seed: int, first_row
         "k": randn(T, cfg["kv_heads"], hd),
         "pos": (torch.randint(0, pos_spec[1], (T,), device=device, dtype=torch.int64, generator=g)
                 if pos_spec[0] == "uniform" else
-                (torch.arange(first_row, first_row + T, device=device) % pos_spec[1])),
+                torch.from_numpy(global_positions(pos_spec, first_row + T)[first_row:]).to(device)),
         "gate": randn(T, cfg["inter"]),
         "up": randn(T, cfg["inter"]),
         **(kv_inputs(T, cfg, device, g) if cfg.get("kv_cache") else {}),
@@ -305,21 +354,44 @@ class ClockSampler:
 # (built from its sources into oracle/_ref) where the reference has the op, and the C/OpenMP
 # restatement (oracle/) for the rest. Host-resident, all host threads.
 
+def synthetic_bf16(rng, n: int, scale: float = 1.0, shift: float = 0.0, block: int = 1 << 24):
+    """n bf16 values (uint16 bits) ~ N(shift, scale^2): one seeded block of up to 16M values,
+    repeated. The repeat period (32 MB) is beyond any CPU cache, so a timed pass over the array
+    does the same work as over fully independent values, and 1M-token inputs take seconds to
+    make instead of minutes."""
+    import numpy as np
+
+    import oracle
+
+    base = oracle.f32_to_bf16(rng.standard_normal(min(n, block), dtype=np.float32) * scale + shift)
+    out = np.empty(n, dtype=np.uint16)
+    for start in range(0, n, base.size):
+        m = min(base.size, n - start)
+        out[start:start + m] = base[:m]
+    return out
+
+
 def cpu_chain_sample(tokens: int, cfg: dict, pos_spec: tuple, steps: int,
                      min_seconds: float = 0.0):
+    """Times `steps` passes of the chain on host memory over `tokens` token rows, with every
+    host thread: the reference's own OpenMP rms_norm (oracle/_ref) for the norms after a LibTorch
+    add that updates the residual in place, as add_rms_norm does, and the C/OpenMP restatement
+    for the ops the reference lacks, writing into preallocated outputs."""
     import numpy as np
     import torch
 
     import oracle
 
     cores = len(os.sched_getaffinity(0))
+    # torchrun exports OMP_NUM_THREADS=1: both OpenMP pools get the cores this line reports
     torch.set_num_threads(cores)
+    threads = oracle.set_num_threads(cores)
     ref = oracle.reference_module()
     rng = np.random.default_rng(1234)
     h, hd, inter = cfg["hidden"], cfg["head_dim"], cfg["inter"]
 
     def bf16(*shape, scale=1.0, shift=0.0):
-        return oracle.f32_to_bf16((rng.standard_normal(shape, dtype=np.float32) * scale + shift))
+        return synthetic_bf16(rng, int(np.prod(shape)), scale, shift).reshape(shape)
 
     table = bf16(cfg["vocab"], h, scale=0.02)
     ids = rng.integers(0, cfg["vocab"], tokens, dtype=np.int32)
@@ -327,8 +399,12 @@ def cpu_chain_sample(tokens: int, cfg: dict, pos_spec: tuple, steps: int,
     q, k = bf16(tokens, cfg["heads"], hd), bf16(tokens, cfg["kv_heads"], hd)
     qw, kw = bf16(hd, scale=0.1, shift=1.0), bf16(hd, scale=0.1, shift=1.0)
     pos = (rng.integers(0, pos_spec[1], tokens, dtype=np.int64) if pos_spec[0] == "uniform"
-           else np.arange(tokens, dtype=np.int64) % pos_spec[1])
+           else global_positions(pos_spec, tokens))
     gate, up = bf16(tokens, inter), bf16(tokens, inter)
+    emb_out = np.empty((tokens, h), dtype=np.uint16)
+    silu_out = np.empty((tokens, inter), dtype=np.uint16)
+    emb_out.fill(0)
+    silu_out.fill(0)  # first-touch the outputs outside the timed passes
     inv = oracle.inv_freq(cfg["theta"], hd, cfg["scaling"])
     names = op_names(cfg)
 
@@ -342,11 +418,11 @@ def cpu_chain_sample(tokens: int, cfg: dict, pos_spec: tuple, steps: int,
     t_start = time.perf_counter()
     while done < steps or time.perf_counter() - t_start < min_seconds:
         t0 = time.perf_counter()
-        oracle.embedding(ids, table)
+        oracle.embedding(ids, table, out=emb_out)
         t1 = time.perf_counter()
         if ref is not None:
-            s = tx + tr  # LibTorch add, then the reference's rms_norm
-            ref.rms_norm(s, tw, cfg["eps"])
+            tr.add_(tx)  # residual <- x + residual (LibTorch), then the reference's rms_norm
+            ref.rms_norm(tr, tw, cfg["eps"])
         else:
             oracle.add_rms_norm(x, r, w, cfg["eps"], inplace=True)
         t2 = time.perf_counter()
@@ -361,7 +437,7 @@ def cpu_chain_sample(tokens: int, cfg: dict, pos_spec: tuple, steps: int,
         else:
             oracle.qk_norm_rope(q, k, qw, kw, pos, cfg["eps"], inv, inplace=True)
         t3 = time.perf_counter()
-        oracle.silu_and_mul(gate, up)
+        oracle.silu_and_mul(gate, up, out=silu_out)
         t4 = time.perf_counter()
         for op, dt in zip(names, (t1 - t0, t2 - t1, t3 - t2, t4 - t3)):
             per_op[op] += dt
@@ -370,10 +446,12 @@ def cpu_chain_sample(tokens: int, cfg: dict, pos_spec: tuple, steps: int,
     total_s = sum(per_op.values())
     gbs = sum(nbytes.values()) * tokens * done / total_s / 1e9
     kind = "reference" if ref is not None else "port"
-    sample = (f"{tokens} tokens x {done} passes of the chain on host memory; "
+    sample = (f"{tokens} tokens x {done} passes of the chain on host memory, {threads} OpenMP "
+              "threads; "
               + ("reference's own OpenMP rms_norm (oracle/_ref, built from its sources) for the "
-                 "norms, after a LibTorch add; C/OpenMP restatement (oracle/) for embedding, "
-                 "rope, silu_and_mul" if ref is not None else "C/OpenMP restatement (oracle/)"))
+                 "norms, after a LibTorch add into the residual; C/OpenMP restatement (oracle/) "
+                 "for embedding, rope, silu_and_mul" if ref is not None
+                 else "C/OpenMP restatement (oracle/)"))
     ops = {op: round(nbytes[op] * tokens * done / per_op[op] / 1e9, 2) for op in names}
     return {"value": round(gbs, 2), "unit": UNIT, "cores": cores, "kind": kind, "sample": sample,
             "ops_gbs": ops, "tokens_per_s": round(tokens * done / total_s, 1),
@@ -402,12 +480,14 @@ def dist_setup(args):
 
 
 def run_reference(args, world, rank) -> int:
-    cfg, total, pos_spec = WORKLOADS[args.workload]
-    total = args.tokens or total
+    """The reference arm: the reference's CPU path over the workload's full token count (the
+    same configuration as the GPU arm), on rank 0 with every host thread."""
+    cfg, _, pos_spec = WORKLOADS[args.workload]
+    total = workload_total(args.workload, args.tokens)
     if rank != 0:
         return 0
-    tokens = min(args.cpu_sample_tokens, total)
-    # untimed warm-up passes, then exactly `steps` timed passes
+    tokens = min(args.reference_tokens, total) if args.reference_tokens else total
+    # untimed warm-up passes on a small slice, then exactly `steps` timed passes
     cpu_chain_sample(min(tokens, 4096), cfg, pos_spec, max(1, args.warmup))
     base = cpu_chain_sample(tokens, cfg, pos_spec, args.steps)
     line = {
@@ -800,6 +880,233 @@ def run_decode_linear(args) -> int:
     return 0
 
 
+# ---------------------------------------------------------------------------------------------
+# The benchmark definition's other configurations, measured in the same run at N=1 (rank 0):
+# config 0 fp32 (GPU through the C ABI's fp32 entry points, CPU through the fp32 restatement),
+# config 1 decode, config 2 packed prefill, config 3 Llama (factors 32 and 8). Each chain pass is
+# replayed from a CUDA graph: at these sizes the host's per-launch cost would otherwise be timed.
+
+class CapiChain:
+    """The chain through the C ABI (svllm_capi): used for fp32, which svllm_ops (bf16 only, like
+    the reference's op API) does not take."""
+
+    def __init__(self, inp: dict, cfg: dict):
+        import torch
+        import svllm_ops
+
+        self.inp, self.cfg = inp, cfg
+        T, dt = inp["ids"].shape[0], inp["x"].dtype
+        dev = inp["ids"].device
+        self.emb_out = torch.empty(T, cfg["hidden"], device=dev, dtype=dt)
+        self.silu_out = torch.empty(T, cfg["inter"], device=dev, dtype=dt)
+        self.inv = svllm_ops.rope_inv_freq(cfg["theta"], cfg["head_dim"], scaling_of(cfg)).tolist()
+
+    def run_op(self, name: str) -> None:
+        import svllm_capi as capi
+
+        i, c = self.inp, self.cfg
+        if name == "embedding":
+            capi.embedding(self.emb_out, i["ids"], i["table"])
+        elif name == "add_rms_norm":
+            capi.add_rms_norm(i["x"], i["residual"], i["w"], c["eps"])
+        elif name == "qk_norm_rope":
+            capi.qk_norm_rope(i["q"], i["k"], i["qw"], i["kw"], i["pos"], c["eps"], self.inv)
+        elif name == "rope":
+            capi.rope(i["q"], i["k"], i["pos"], self.inv)
+        else:
+            capi.silu_and_mul(self.silu_out, i["gate"], i["up"])
+
+
+def graph_chain_us(chain, names: list[str], reps: int, warmup: int) -> float:
+    """Microseconds per pass of the chain, `reps` passes captured in one CUDA graph and the
+    graph replayed (after `warmup` eager passes and one untimed replay)."""
+    import torch
+
+    for _ in range(max(1, warmup)):
+        for op in names:
+            chain.run_op(op)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    capture = torch.cuda.Stream()
+    capture.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(capture):
+        with torch.cuda.graph(graph, stream=capture):
+            for _ in range(reps):
+                for op in names:
+                    chain.run_op(op)
+    torch.cuda.current_stream().wait_stream(capture)
+    graph.replay()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    replays = 3
+    start.record()
+    for _ in range(replays):
+        graph.replay()
+    stop.record()
+    torch.cuda.synchronize()
+    del graph
+    return start.elapsed_time(stop) * 1e3 / (replays * reps)
+
+
+def cpu_fp32_chain(tokens: int, cfg: dict, pos_hi: int, steps: int) -> dict:
+    """Config 0's CPU side: the fp32 chain through the C/OpenMP restatement (the reference has
+    no fp32 kernel: its op API rejects fp32) with every host thread."""
+    import numpy as np
+
+    import oracle
+
+    cores = len(os.sched_getaffinity(0))
+    threads = oracle.set_num_threads(cores)
+    rng = np.random.default_rng(99)
+    h, hd, inter = cfg["hidden"], cfg["head_dim"], cfg["inter"]
+
+    def f32(*shape, scale=1.0, shift=0.0):
+        return (rng.standard_normal(shape, dtype=np.float32) * scale + shift).astype(np.float32)
+
+    table = f32(cfg["vocab"], h, scale=0.02)
+    ids = rng.integers(0, cfg["vocab"], tokens, dtype=np.int32)
+    x, r, w = f32(tokens, h), f32(tokens, h), f32(h, scale=0.1, shift=1.0)
+    q, k = f32(tokens, cfg["heads"], hd), f32(tokens, cfg["kv_heads"], hd)
+    qw, kw = f32(hd, scale=0.1, shift=1.0), f32(hd, scale=0.1, shift=1.0)
+    pos = rng.integers(0, pos_hi, tokens, dtype=np.int64)
+    gate, up = f32(tokens, inter), f32(tokens, inter)
+    emb_out, silu_out = np.empty((tokens, h), np.float32), np.empty((tokens, inter), np.float32)
+    inv = oracle.inv_freq(cfg["theta"], hd, cfg["scaling"])
+
+    def chain():
+        oracle.embedding(ids, table, out=emb_out)
+        oracle.add_rms_norm(x, r, w, cfg["eps"], inplace=True)
+        oracle.qk_norm_rope(q, k, qw, kw, pos, cfg["eps"], inv, inplace=True)
+        oracle.silu_and_mul(gate, up, out=silu_out)
+
+    chain()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        chain()
+    sec = (time.perf_counter() - t0) / steps
+    nbytes = sum(op_bytes(cfg, elem=4).values()) * tokens
+    return {"value": round(nbytes / sec / 1e9, 2), "unit": UNIT, "cores": cores, "kind": "port",
+            "us_per_chain": round(sec * 1e6, 1),
+            "sample": f"{tokens} tokens x {steps} passes of the fp32 chain on host memory, "
+                      f"{threads} OpenMP threads; C/OpenMP restatement (oracle/): the reference "
+                      "rejects fp32"}
+
+
+def measure_configs(args, dev, peak: float) -> dict:
+    """Configs 0-3 of the benchmark definition at their own sizes, one CUDA-graph timing each,
+    with the SM clock sampled around it."""
+    import torch
+
+    out = {}
+    cases = [
+        ("config0_fp32", "decode", dict(QWEN3), torch.float32),
+        ("config1_decode", "decode", dict(QWEN3), torch.bfloat16),
+        ("config2_prefill", "prefill", dict(QWEN3), torch.bfloat16),
+        ("config3_llama_factor32", "llama", dict(LLAMA), torch.bfloat16),
+        ("config3_llama_factor8", "llama", dict(LLAMA, scaling=(8.0, 1.0, 4.0, 8192)),
+         torch.bfloat16),
+    ]
+    for key, workload, cfg, dtype in cases:
+        _, _, pos_spec = WORKLOADS[workload]
+        if key == "config0_fp32":
+            pos_spec = ("packed", 256)  # positions 0..255
+        T = workload_total(workload)
+        inp = make_inputs(T, pos_spec, cfg, dev, seed=4242)
+        if dtype == torch.float32:
+            inp = {k: (v.float() if v.dtype == torch.bfloat16 else v) for k, v in inp.items()}
+            chain = CapiChain(inp, cfg)
+        else:
+            chain = Chain(inp, cfg)
+        names = op_names(cfg)
+        reps = 20 if T <= 4096 else 2
+        sampler = ClockSampler([dev.index])
+        with sampler:
+            us = graph_chain_us(chain, names, reps, args.warmup)
+        nbytes = sum(op_bytes(cfg, elem=4 if dtype == torch.float32 else 2).values()) * T
+        gbs = nbytes / (us * 1e-6) / 1e9
+        entry = {
+            "tokens": T, "dtype": "f32" if dtype == torch.float32 else "bf16",
+            "positions": positions_label(pos_spec), "ops": names,
+            "rope_scaling": cfg["scaling"], "us_per_chain": round(us, 2),
+            "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4),
+            "tokens_per_s": round(T / (us * 1e-6), 1), "cuda_graph": True,
+            "l2": ("inputs L2-resident (decode-sized; not flushed)" if nbytes < 126e6 else
+                   "each pass streams more than the 126 MB L2"),
+            "clocks": sampler.summary(),
+        }
+        if key == "config0_fp32" and not args.no_cpu_baseline:
+            entry["cpu_baseline"] = cpu_fp32_chain(T, cfg, 4096, max(20, args.steps))
+        out[key] = entry
+        del chain, inp
+        torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
+# RMSNorm alone, the one op the reference ships a CUDA kernel for: svllm_ops.rms_norm (--impl
+# ours) or the reference's own op API on its own CUDA kernel, built from its sources into
+# oracle/_ref (--impl reference), timed the same way on the same shapes.
+
+RMS_SHAPES = [(1_048_576, 1024), (16_384, 2048), (1_048_576 * 16, 128)]
+
+
+def run_rms_norm(args) -> int:
+    import torch
+
+    dev = torch.device("cuda", 0)
+    if args.impl == "reference":
+        import oracle
+
+        op = oracle.reference_module()
+        if op is None:
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the reference's rms_norm was not built into oracle/_ref"}))
+            return 0
+        fn, label = op.rms_norm, "reference CUDA rms_norm (its src/ops/cuda/rms_norm.cu, sm_100a)"
+    else:
+        import svllm_ops
+
+        fn, label = svllm_ops.rms_norm, "svllm_ops.rms_norm (sm_100a bulk-copy kernel)"
+    g = torch.Generator(device=dev).manual_seed(17)
+    peak = float(measured_peaks()["hbm_gbs"])
+    shapes = {}
+    sampler = ClockSampler([0])
+    with sampler:
+        for rows, hidden in RMS_SHAPES:
+            x = torch.empty(rows, hidden, device=dev, dtype=torch.bfloat16).normal_(generator=g)
+            w = (torch.empty(hidden, device=dev).normal_(generator=g) * 0.1 + 1).to(torch.bfloat16)
+            for _ in range(args.warmup):
+                fn(x, w, 1e-6)
+            torch.cuda.synchronize()
+            start = torch.cuda.Event(enable_timing=True)
+            stop = torch.cuda.Event(enable_timing=True)
+            start.record()
+            for _ in range(args.steps):
+                fn(x, w, 1e-6)
+            stop.record()
+            torch.cuda.synchronize()
+            ms = start.elapsed_time(stop) / args.steps
+            nbytes = rows * hidden * 4  # read x, write out (bf16); the weight is amortised
+            shapes[f"{rows}x{hidden}"] = {"ms": round(ms, 4),
+                                          "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                                          "frac_of_peak": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4)}
+            del x
+            torch.cuda.empty_cache()
+    head = shapes[f"{RMS_SHAPES[0][0]}x{RMS_SHAPES[0][1]}"]
+    line = {"metric": "rms_norm achieved HBM GB/s", "value": head["gbs"], "unit": UNIT,
+            "impl": args.impl, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": head["ms"], "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "rms_norm, bf16, x ~ N(0,1), weight 1+N(0,0.1), eps 1e-6",
+                       "shapes": [f"{r}x{h}" for r, h in RMS_SHAPES],
+                       "timing": "CUDA events around `steps` back-to-back calls of the op API "
+                                 "(output allocation included, as the API allocates it)",
+                       "l2": "inputs larger than L2 except 16384x2048 (67 MB: L2-warm)"},
+            "op": label, "shapes": shapes, "peak": peak, "clocks": sampler.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main() -> int:
     args = parse_args()
     if args.workload == "sampling":
@@ -812,6 +1119,8 @@ def main() -> int:
         return run_decode_attention(args)
     if args.workload == "decode-linear":
         return run_decode_linear(args)
+    if args.workload == "rms-norm":
+        return run_rms_norm(args)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)
@@ -824,8 +1133,8 @@ def main() -> int:
     assert torch.cuda.is_available(), "bench.py (impl ours) needs a GPU"
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    cfg, total, pos_spec = WORKLOADS[args.workload]
-    total = args.tokens or total
+    cfg, _, pos_spec = WORKLOADS[args.workload]
+    total = workload_total(args.workload, args.tokens)
     if args.kv_cache:
         # the cache variant is measured on the device; e2e, the CPU leg and validation cover the
         # headline chain
@@ -923,6 +1232,10 @@ def main() -> int:
         cpu = cpu_chain_sample(min(args.cpu_sample_tokens, total), cfg, pos_spec, 2,
                                min_seconds=5.0)
 
+    configs = None
+    if rank == 0 and world == 1 and args.workload == "sweep" and not args.no_configs:
+        configs = measure_configs(args, dev, float(measured_peaks()["hbm_gbs"]))
+
     if rank == 0:
         peaks = measured_peaks()
         peak = float(peaks["hbm_gbs"])
@@ -941,8 +1254,7 @@ def main() -> int:
                        "tokens": total, "tokens_per_gpu": T, "hidden": cfg["hidden"],
                        "heads": [cfg["heads"], cfg["kv_heads"]], "head_dim": cfg["head_dim"],
                        "intermediate": cfg["inter"], "vocab": cfg["vocab"],
-                       "positions": (f"uniform [0, {pos_spec[1]})" if pos_spec[0] == "uniform"
-                                     else f"sequences of {pos_spec[1]}, positions 0..{pos_spec[1] - 1}"),
+                       "positions": positions_label(pos_spec),
                        "rope_scaling": cfg["scaling"], "ops": names,
                        "l2": "no flush: every op's inputs exceed the 126 MB L2"
                        if T * 2 * cfg["hidden"] > 126e6 else "inputs L2-resident (small T)",
@@ -973,6 +1285,7 @@ def main() -> int:
             "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
             if cpu else None,
             "validation": validation,
+            "configs": configs,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -995,14 +1308,75 @@ def load_traffic(kernel_op: str, tokens: int):
 
 
 # ---------------------------------------------------------------------------------------------
-# Validation (outside every timed region): the first rows of every rank's shard, inputs and
-# outputs, are all-gathered to rank 0 (NCCL, the one collective of the sharded run) and recomputed
-# there by svllm_ops' CPU backend. The embedding and the residual add must agree bit for bit;
-# the other outputs within 2 bf16 ulp, or within 2^-7 of their row's largest magnitude where a
-# rotation cancels (the CPU's cosf/sinf/expf are the C library's, not CUDA's).
+# Validation (outside every timed region), against two references:
+#   * the same GPU's torch composites of the formulas, on every rank: index_select for the
+#     gather, a bf16 add for the residual, the reference test's own RMSNorm composite
+#     (tests/python/test_rms_norm.py:24-27: F.rms_norm in fp32, rounded, times the weight) for the
+#     norms, Hugging Face's rotary embedding, F.silu(gate) * up. The gather, the residual and
+#     SiLU * up must agree bit for bit; the norms differ from the composite only in summation
+#     order (the kernels replay the reference CUDA kernel's), so those outputs are held to 2 bf16
+#     ulp or 2^-7 of the row's largest magnitude, and their max-abs error is reported;
+#   * svllm_ops' CPU backend on rank 0, after an NCCL all-gather of every rank's first rows
+#     (the one collective of the sharded run), under the same bars (the CPU's cosf/sinf/expf are
+#     the C library's, not CUDA's).
+
+def _compare(got, want, exact: bool) -> dict:
+    import numpy as np
+    import torch
+
+    def bits(t):
+        return t.contiguous().cpu().view(torch.int16).numpy().view(np.uint16).astype(np.int32)
+
+    a, b = bits(got), bits(want)
+    ulp = np.abs(np.where(a & 0x8000, -(a & 0x7FFF), a) - np.where(b & 0x8000, -(b & 0x7FFF), b))
+    av, bv = got.float().cpu().numpy(), want.float().cpu().numpy()
+    flat_b = np.abs(bv).reshape(bv.shape[0], -1).max(axis=1)
+    tol = (2.0 ** -7 * flat_b).reshape((-1,) + (1,) * (bv.ndim - 1))
+    within = (ulp <= 2) | (np.abs(av - bv) <= tol)
+    good = bool((ulp == 0).all()) if exact else bool(within.all())
+    scale = np.maximum(flat_b, np.finfo(np.float32).tiny).reshape(tol.shape)
+    return {"worst_bf16_ulp": int(ulp.max()), "not_bit_exact": int((ulp > 0).sum()),
+            "max_abs": float(np.abs(av - bv).max()),
+            "worst_abs_err_over_row_max": float((np.abs(av - bv) / scale).max()),
+            "bit_exact_required": exact, "ok": good}
+
+
+def torch_composites(saved: dict, inp: dict, cfg: dict) -> dict:
+    """The chain's outputs for the saved inputs, by torch ops on the inputs' device."""
+    import torch
+    import torch.nn.functional as F
+
+    import svllm_ops
+
+    eps, d = cfg["eps"], cfg["head_dim"]
+    bf = torch.bfloat16
+
+    def norm(x, w):
+        return F.rms_norm(x.float(), (x.shape[-1],), eps=eps).to(bf) * w
+
+    inv = svllm_ops.rope_inv_freq(cfg["theta"], d, scaling_of(cfg)).to(saved["q"].device)
+
+    def rope(x, pos):
+        freqs = pos.float()[:, None] * inv[None, :]
+        emb = torch.cat((freqs, freqs), dim=-1)
+        cos, sin = emb.cos().to(bf)[:, None, :], emb.sin().to(bf)[:, None, :]
+        half = x.shape[-1] // 2
+        return x * cos + torch.cat((-x[..., half:], x[..., :half]), dim=-1) * sin
+
+    r = saved["x"] + saved["residual"]
+    q, k = saved["q"], saved["k"]
+    if cfg["qk_norm"]:
+        q, k = norm(q, inp["qw"]), norm(k, inp["kw"])
+    return {"embedding": inp["table"].index_select(0, saved["ids"].long()),
+            "x": norm(r, inp["w"]), "residual": r,
+            "q": rope(q, saved["pos"]), "k": rope(k, saved["pos"]),
+            "silu": F.silu(saved["gate"]) * saved["up"]}
+
+
+EXACT_OUTPUTS = ("embedding", "residual", "silu")
+
 
 def validate(chain, inp, cfg, world, rank, dev, rows: int = 256):
-    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -1021,6 +1395,21 @@ def validate(chain, inp, cfg, world, rank, dev, rows: int = 256):
     torch.cuda.synchronize()
     got = {"embedding": chain.emb_out[:n], "x": inp["x"][:n], "residual": inp["residual"][:n],
            "q": inp["q"][:n], "k": inp["k"][:n], "silu": chain.silu_out[:n]}
+
+    # every rank against its own GPU's torch composites; the worst over ranks is reported
+    comp = torch_composites(saved, inp, cfg)
+    gpu_report = {name: _compare(got[name], comp[name], name in EXACT_OUTPUTS) for name in got}
+    if world > 1:
+        for name, rep in gpu_report.items():
+            v = torch.tensor([rep["worst_bf16_ulp"], rep["not_bit_exact"], rep["max_abs"],
+                              rep["worst_abs_err_over_row_max"], 0.0 if rep["ok"] else 1.0],
+                             device=dev, dtype=torch.float64)
+            mx = v.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            dist.all_reduce(v, op=dist.ReduceOp.SUM)
+            rep.update({"worst_bf16_ulp": int(mx[0]), "not_bit_exact": int(v[1]),
+                        "max_abs": float(mx[2]), "worst_abs_err_over_row_max": float(mx[3]),
+                        "ok": bool(mx[4] == 0)})
 
     def gather(t):
         return svllm_dist.all_gather_rows(t.contiguous(), n * world) if world > 1 else t
@@ -1042,30 +1431,11 @@ def validate(chain, inp, cfg, world, rank, dev, rows: int = 256):
         ops.rope(q, k, ins["pos"], cfg["theta"], scaling_of(cfg))
     y = ops.silu_and_mul(ins["gate"], ins["up"])
     want = {"embedding": emb, "x": x, "residual": r, "q": q, "k": k, "silu": y}
-
-    def bits(t):
-        return t.contiguous().view(torch.int16).numpy().view(np.uint16).astype(np.int32)
-
-    report, ok = {}, True
-    for name in want:
-        a, b = bits(got[name]), bits(want[name])
-        ulp = np.abs(np.where(a & 0x8000, -(a & 0x7FFF), a) - np.where(b & 0x8000, -(b & 0x7FFF), b))
-        av = got[name].float().numpy()
-        bv = want[name].float().numpy()
-        flat_b = np.abs(bv).reshape(bv.shape[0], -1).max(axis=1)
-        tol = (2.0 ** -7 * flat_b).reshape((-1,) + (1,) * (bv.ndim - 1))
-        # a rotation output that cancels to near zero can be many ulps off in its own scale and
-        # still within one rounding of the terms it came from: held to 2^-7 of the row's largest
-        within = (ulp <= 2) | (np.abs(av - bv) <= tol)
-        exact_needed = name in ("embedding", "residual")
-        good = bool((ulp == 0).all()) if exact_needed else bool(within.all())
-        ok = ok and good
-        scale = np.maximum(flat_b, np.finfo(np.float32).tiny).reshape(tol.shape)
-        report[name] = {"worst_bf16_ulp": int(ulp.max()), "not_bit_exact": int((ulp > 0).sum()),
-                        "worst_abs_err_over_row_max": float((np.abs(av - bv) / scale).max()),
-                        "ok": good}
-    return {"rows_per_gpu": n, "gathered_from": world, "against": "svllm_ops CPU backend",
-            "ops": report, "ok": ok}
+    cpu_report = {name: _compare(got[name], want[name], name in ("embedding", "residual"))
+                  for name in want}
+    ok = all(v["ok"] for v in gpu_report.values()) and all(v["ok"] for v in cpu_report.values())
+    return {"rows_per_gpu": n, "gathered_from": world,
+            "same_gpu_torch_composites": gpu_report, "cpu_backend": cpu_report, "ok": ok}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -1074,9 +1444,15 @@ def validate(chain, inp, cfg, world, rank, dev, rows: int = 256):
 # while the kernels work. Every step copies all of that step's inputs in and outputs out.
 
 def measure_e2e(chain, inp, cfg, args, world, dev):
+    """The chain end to end through the C ABI (svllm_capi: the drop-in boundary a host program
+    binds) from and to pinned host buffers: every step copies each chunk's inputs in, runs the
+    four ops on the chunk (the gather and SiLU writing straight into the device buffers that are
+    copied out), and copies every output back; copies and kernels overlap across chunks on
+    three streams."""
     import torch
     import torch.distributed as dist
 
+    import svllm_capi as capi
     import svllm_ops
 
     T = inp["ids"].shape[0]
@@ -1094,6 +1470,7 @@ def measure_e2e(chain, inp, cfg, args, world, dev):
     emb_dev = torch.empty(T, cfg["hidden"], device=dev, dtype=torch.bfloat16)
     h2d = sum(t.numel() * t.element_size() for t in host_in.values())
     d2h = sum(t.numel() * t.element_size() for t in host_out.values())
+    inv = svllm_ops.rope_inv_freq(cfg["theta"], cfg["head_dim"], scaling_of(cfg)).tolist()
 
     chunks = max(1, min(16, T // 16384))
     bounds = [(T * c // chunks, T * (c + 1) // chunks) for c in range(chunks)]
@@ -1116,17 +1493,14 @@ def measure_e2e(chain, inp, cfg, args, world, dev):
                 done_in.append(e)
         for c, (a, b) in enumerate(bounds):
             s_comp.wait_event(done_in[c])
-            emb = svllm_ops.embedding(inp["ids"][a:b], inp["table"])
-            emb_dev[a:b].copy_(emb, non_blocking=True)
-            svllm_ops.add_rms_norm(inp["x"][a:b], inp["residual"][a:b], inp["w"], cfg["eps"])
+            capi.embedding(emb_dev[a:b], inp["ids"][a:b], inp["table"])
+            capi.add_rms_norm(inp["x"][a:b], inp["residual"][a:b], inp["w"], cfg["eps"])
             if cfg["qk_norm"]:
-                svllm_ops.qk_norm_rope(inp["q"][a:b], inp["k"][a:b], inp["qw"], inp["kw"],
-                                       inp["pos"][a:b], cfg["eps"], cfg["theta"], scaling_of(cfg))
+                capi.qk_norm_rope(inp["q"][a:b], inp["k"][a:b], inp["qw"], inp["kw"],
+                                  inp["pos"][a:b], cfg["eps"], inv)
             else:
-                svllm_ops.rope(inp["q"][a:b], inp["k"][a:b], inp["pos"][a:b], cfg["theta"],
-                               scaling_of(cfg))
-            silu_dev[a:b].copy_(svllm_ops.silu_and_mul(inp["gate"][a:b], inp["up"][a:b]),
-                                non_blocking=True)
+                capi.rope(inp["q"][a:b], inp["k"][a:b], inp["pos"][a:b], inv)
+            capi.silu_and_mul(silu_dev[a:b], inp["gate"][a:b], inp["up"][a:b])
             e = torch.cuda.Event()
             e.record(s_comp)
             done_comp.append(e)
@@ -1168,18 +1542,21 @@ def measure_e2e(chain, inp, cfg, args, world, dev):
         dist.all_reduce(tt)
         total = int(tt.item())
     value = sum(op_bytes(cfg).values()) * total / (ms * 1e-3) / 1e9
-    bound = pcie_bound_ms(dev, h2d, d2h)
+    # the PCIe bound with every rank copying at once, as they do in the timed steps
+    bound = pcie_bound_ms(dev, h2d, d2h, world)
     return {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d * world,
             "d2h_bytes_per_step": d2h * world, "ms_per_step": round(ms, 3),
-            "chunks": chunks, "api": "svllm_ops (pinned host buffers, 3 streams)",
+            "chunks": chunks, "api": "C ABI through svllm_capi (pinned host buffers, 3 streams)",
             "pcie": {**bound, "frac": round(bound["bound_ms"] / ms, 4)}}
 
 
-def pcie_bound_ms(dev, h2d: int, d2h: int) -> dict:
+def pcie_bound_ms(dev, h2d: int, d2h: int, world: int = 1) -> dict:
     """The step time PCIe alone allows: pinned-buffer copies measured here, one direction alone
-    and both at once; the copy-out overlaps the copy-in at the two-way rate, the rest of the
-    larger direction runs at the one-way rate."""
+    and both at once, with every rank copying at the same time (a barrier starts each
+    measurement; the slowest rank's rate counts); the copy-out overlaps the copy-in at the
+    two-way rate, the rest of the larger direction runs at the one-way rate."""
     import torch
+    import torch.distributed as dist
 
     n = 1 << 29
     hs = [torch.empty(n, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
@@ -1189,11 +1566,16 @@ def pcie_bound_ms(dev, h2d: int, d2h: int) -> dict:
     def timed(fn) -> float:
         fn()
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         t0 = time.perf_counter()
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
-        return (time.perf_counter() - t0) / 3
+        sec = torch.tensor([(time.perf_counter() - t0) / 3], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(sec, op=dist.ReduceOp.MAX)
+        return float(sec.item())
 
     def one_way():
         with torch.cuda.stream(s_in):
@@ -1210,7 +1592,7 @@ def pcie_bound_ms(dev, h2d: int, d2h: int) -> dict:
     small, large = sorted((h2d, d2h))
     bound_s = small / both + (large - small) / one
     return {"one_way_gbs": round(one / 1e9, 1), "two_way_gbs_each": round(both / 1e9, 1),
-            "bound_ms": round(bound_s * 1e3, 1)}
+            "bound_ms": round(bound_s * 1e3, 1), "ranks_copying_at_once": world}
 
 
 if __name__ == "__main__":
