@@ -153,7 +153,12 @@ __device__ __forceinline__ int64_t load_slot(const RopeArgs& a, int64_t t) {
 // 16-byte vectors of a token's v row each lane holds in registers (a 2 KB row per warp).
 constexpr int kVRegs = 4;
 
-template <class E, int G, bool kNorm, bool kCache>
+// kPasses > 0: the token's heads take exactly kPasses passes of kWarpSize / G heads and the q heads
+// fill whole passes, so the pass loop is unrolled and each pass is all-q or all-k (one weight,
+// no per-lane select); the compiler interleaves the passes' independent chains. Measured on a
+// B200 at 1M tokens of the Qwen3-0.6B shapes: 6586 GB/s against 6396 for the runtime loop.
+// kPasses == 0: a runtime loop over any number of heads.
+template <class E, int G, bool kNorm, bool kCache, int kPasses>
 __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ RopeArgs a) {
   grid_dependency_sync();
   using S = typename E::Storage;
@@ -265,13 +270,15 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
     const uint8_t* st = ring + static_cast<size_t>(stage) * a.stage_bytes;
     const int64_t t = wu.at(j);
 
-    for (int h0 = 0; h0 < total_heads; h0 += kHeadsPerPass) {
+    // One pass: heads h0 .. h0 + kHeadsPerPass - 1, lane / G picking the head. q_pass: the
+    // pass is all q heads (kPasses > 0), else each lane checks its own head.
+    auto head_pass = [&](int h0, bool q_pass) {
       const int h = h0 + lane / G;
       const bool valid = h < total_heads;
       const uint8_t* hs = st + static_cast<size_t>(valid ? h : 0) * kDim * sizeof(S);
       uint4 lo = ld_shared_v4(hs + sub * 16);
       uint4 hi = ld_shared_v4(hs + kHalf * sizeof(S) + sub * 16);
-      const bool is_q = h < num_heads;
+      const bool is_q = kPasses > 0 ? q_pass : h < num_heads;
       if constexpr (kNorm) {
         // The head's sum of squares in the order of the reference's rms_norm kernel run on the
         // [tokens * heads, head_dim] view: lane j holds that kernel's vectors j (lo) and j + G
@@ -313,6 +320,12 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
           }
         }
       }
+    };
+    if constexpr (kPasses > 0) {
+#pragma unroll
+      for (int p = 0; p < kPasses; ++p) head_pass(p * kHeadsPerPass, p * kHeadsPerPass < num_heads);
+    } else {
+      for (int h0 = 0; h0 < total_heads; h0 += kHeadsPerPass) head_pass(h0, false);
     }
     if constexpr (kCache) {
       if (slot >= 0) {
@@ -447,15 +460,27 @@ __global__ void __launch_bounds__(256) rope_plain_kernel(const __grid_constant__
 using RopeKernel = void (*)(RopeArgs);
 
 template <class E, bool kNorm, bool kCache>
-RopeKernel pick_bulk_kernel(int head_dim) {
+RopeKernel pick_bulk_kernel(int head_dim, int num_heads, int num_kv_heads) {
   constexpr int kVec = E::kPerVec;
   if (head_dim % (2 * kVec) != 0) return nullptr;
-  switch (head_dim / (2 * kVec)) {
-    case 2: return rope_bulk_kernel<E, 2, kNorm, kCache>;
-    case 4: return rope_bulk_kernel<E, 4, kNorm, kCache>;
-    case 8: return rope_bulk_kernel<E, 8, kNorm, kCache>;
-    case 16: return rope_bulk_kernel<E, 16, kNorm, kCache>;
-    case 32: return rope_bulk_kernel<E, 32, kNorm, kCache>;
+  const int g = head_dim / (2 * kVec);
+  const int per_pass = g > 0 && g <= kWarpSize ? kWarpSize / g : 0;
+  const int total = num_heads + num_kv_heads;
+  // unrolled kernels for the head layouts of the Qwen3 (24 or 40 heads of 128) and Llama-3.2
+  // (40 heads of 64) families: bf16, q heads filling whole passes
+  const bool whole = per_pass > 0 && num_heads % per_pass == 0 && total % per_pass == 0;
+  const int passes = whole ? total / per_pass : 0;
+  if constexpr (sizeof(typename E::Storage) == 2) {
+    if (g == 8 && passes == 6) return rope_bulk_kernel<E, 8, kNorm, kCache, 6>;
+    if (g == 8 && passes == 10) return rope_bulk_kernel<E, 8, kNorm, kCache, 10>;
+    if (g == 4 && passes == 5) return rope_bulk_kernel<E, 4, kNorm, kCache, 5>;
+  }
+  switch (g) {
+    case 2: return rope_bulk_kernel<E, 2, kNorm, kCache, 0>;
+    case 4: return rope_bulk_kernel<E, 4, kNorm, kCache, 0>;
+    case 8: return rope_bulk_kernel<E, 8, kNorm, kCache, 0>;
+    case 16: return rope_bulk_kernel<E, 16, kNorm, kCache, 0>;
+    case 32: return rope_bulk_kernel<E, 32, kNorm, kCache, 0>;
     default: return nullptr;
   }
 }
@@ -547,7 +572,10 @@ int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
       (!kCache || (aligned16(cache.v) && (cache.v_stride * sizeof(S)) % 16 == 0 &&
                    aligned16(cache.k_cache) && aligned16(cache.v_cache)));
   const RopeKernel kernel =
-      bulk_ok ? pick_bulk_kernel<E, kNorm, kCache>(static_cast<int>(head_dim)) : nullptr;
+      bulk_ok ? pick_bulk_kernel<E, kNorm, kCache>(static_cast<int>(head_dim),
+                                                   static_cast<int>(num_heads),
+                                                   static_cast<int>(num_kv_heads))
+              : nullptr;
   if (kernel != nullptr) {
     const PipelineShape shape = pipeline_shape(kNorm ? OpId::kQkNormRope : OpId::kRope);
     a.stage_bytes = static_cast<int>(round_up(q_bytes + k_bytes, 128));  // v is not staged
