@@ -1070,9 +1070,11 @@ def run_rms_norm(args) -> int:
     g = torch.Generator(device=dev).manual_seed(17)
     peak = float(measured_peaks()["hbm_gbs"])
     shapes = {}
+    # --tokens N: one shape, N rows of 1024 (a small case for a profiler)
+    run_shapes = [(args.tokens, 1024)] if args.tokens else RMS_SHAPES
     sampler = ClockSampler([0])
     with sampler:
-        for rows, hidden in RMS_SHAPES:
+        for rows, hidden in run_shapes:
             x = torch.empty(rows, hidden, device=dev, dtype=torch.bfloat16).normal_(generator=g)
             w = (torch.empty(hidden, device=dev).normal_(generator=g) * 0.1 + 1).to(torch.bfloat16)
             for _ in range(args.warmup):
@@ -1092,13 +1094,13 @@ def run_rms_norm(args) -> int:
                                           "frac_of_peak": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4)}
             del x
             torch.cuda.empty_cache()
-    head = shapes[f"{RMS_SHAPES[0][0]}x{RMS_SHAPES[0][1]}"]
+    head = shapes[f"{run_shapes[0][0]}x{run_shapes[0][1]}"]
     line = {"metric": "rms_norm achieved HBM GB/s", "value": head["gbs"], "unit": UNIT,
             "impl": args.impl, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": head["ms"], "higher_is_better": True, "dtype": "bf16",
             "data": "synthetic",
             "config": {"workload": "rms_norm, bf16, x ~ N(0,1), weight 1+N(0,0.1), eps 1e-6",
-                       "shapes": [f"{r}x{h}" for r, h in RMS_SHAPES],
+                       "shapes": [f"{r}x{h}" for r, h in run_shapes],
                        "timing": "CUDA events around `steps` back-to-back calls of the op API "
                                  "(output allocation included, as the API allocates it)",
                        "l2": "inputs larger than L2 except 16384x2048 (67 MB: L2-warm)"},
