@@ -477,42 +477,44 @@ int pick_bn(int64_t m, int64_t n, int sms) {
   return best;
 }
 
-}  // namespace
-}  // namespace svllm::k
-
-extern "C" int svllm_lm_head_argmax_bf16(const void* hidden, int64_t num_rows,
-                                         int64_t hidden_size, int64_t hidden_stride,
-                                         const void* weight, int64_t vocab, int64_t weight_stride,
-                                         int64_t* out_ids, void* logits, int64_t logits_stride,
-                                         void* workspace, int64_t workspace_bytes,
-                                         svllm_stream stream) {
-  using namespace svllm::k;
+// Size checks shared by both entry points (SVLLM_OK: the arguments describe a valid call).
+int check_lm_head_sizes(int64_t num_rows, int64_t hidden_size, int64_t hidden_stride,
+                        int64_t vocab, int64_t weight_stride, const void* logits,
+                        int64_t logits_stride) {
   if (num_rows < 0 || hidden_size <= 0 || vocab <= 0 || hidden_stride < hidden_size ||
       weight_stride < hidden_size || vocab >= (int64_t{1} << 31) ||
       num_rows >= (int64_t{1} << 31) || (logits != nullptr && logits_stride < vocab)) {
     return SVLLM_ERR_INVALID_ARGUMENT;
   }
-  if (num_rows == 0) return SVLLM_OK;
-  if (hidden == nullptr || weight == nullptr || out_ids == nullptr || workspace == nullptr ||
-      workspace_bytes < num_rows * static_cast<int64_t>(sizeof(uint64_t))) {
+  return SVLLM_OK;
+}
+
+// Pointer checks shared by both entry points: present, and the 16-byte aligned bases and row
+// strides the tensor maps want.
+int check_lm_head_operands(const void* hidden, int64_t hidden_stride, const void* weight,
+                           int64_t weight_stride, const int64_t* out_ids) {
+  if (hidden == nullptr || weight == nullptr || out_ids == nullptr) {
     return SVLLM_ERR_INVALID_ARGUMENT;
   }
-  // the tensor maps want 16-byte aligned bases and row strides; the workspace 8-byte keys
   if (!aligned16(hidden) || !aligned16(weight) || (hidden_stride * 2) % 16 != 0 ||
-      (weight_stride * 2) % 16 != 0 || (reinterpret_cast<uintptr_t>(workspace) & 7u) != 0) {
+      (weight_stride * 2) % 16 != 0) {
     return SVLLM_ERR_UNSUPPORTED;
   }
-  int device;
-  if (current_device(&device) != SVLLM_OK) return SVLLM_ERR_CUDA;
-  int* err = library_error_word(device);
-  if (err == nullptr) return SVLLM_ERR_CUDA;
-  const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return SVLLM_OK;
+}
 
+// The GEMM with its argmax epilogue into `keys` (num_rows zeroed 8-byte keys), then the kernel
+// that turns keys into ids and zeroes them again. Arguments already checked.
+int run_lm_head_argmax(const void* hidden, int64_t num_rows, int64_t hidden_size,
+                       int64_t hidden_stride, const void* weight, int64_t vocab,
+                       int64_t weight_stride, int64_t* out_ids, void* logits,
+                       int64_t logits_stride, uint64_t* keys, int device, int* err,
+                       cudaStream_t s) {
   LmHeadArgs a{};
   a.m = num_rows;
   a.n = vocab;
   a.k = hidden_size;
-  a.keys = static_cast<uint64_t*>(workspace);
+  a.keys = keys;
   a.logits = logits;
   a.logits_stride = logits_stride;
   a.err = err;
@@ -530,7 +532,37 @@ extern "C" int svllm_lm_head_argmax_bf16(const void* hidden, int64_t num_rows,
   if (status != SVLLM_OK) return status;
   const int64_t blocks = (num_rows + 255) / 256;
   return launch(lm_head_argmax_finish_kernel, dim3(static_cast<unsigned>(blocks < 1024 ? blocks : 1024)),
-                dim3(256), 0, s, 1, a.keys, num_rows, out_ids);
+                dim3(256), 0, s, 1, keys, num_rows, out_ids);
+}
+
+}  // namespace
+}  // namespace svllm::k
+
+extern "C" int svllm_lm_head_argmax_bf16(const void* hidden, int64_t num_rows,
+                                         int64_t hidden_size, int64_t hidden_stride,
+                                         const void* weight, int64_t vocab, int64_t weight_stride,
+                                         int64_t* out_ids, void* logits, int64_t logits_stride,
+                                         void* workspace, int64_t workspace_bytes,
+                                         svllm_stream stream) {
+  using namespace svllm::k;
+  int status = check_lm_head_sizes(num_rows, hidden_size, hidden_stride, vocab, weight_stride,
+                                   logits, logits_stride);
+  if (status != SVLLM_OK) return status;
+  if (num_rows == 0) return SVLLM_OK;
+  if (workspace == nullptr || workspace_bytes < num_rows * static_cast<int64_t>(sizeof(uint64_t))) {
+    return SVLLM_ERR_INVALID_ARGUMENT;
+  }
+  status = check_lm_head_operands(hidden, hidden_stride, weight, weight_stride, out_ids);
+  if (status != SVLLM_OK) return status;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 7u) != 0) return SVLLM_ERR_UNSUPPORTED;  // 8-byte keys
+  int device;
+  if (current_device(&device) != SVLLM_OK) return SVLLM_ERR_CUDA;
+  int* err = library_error_word(device);
+  if (err == nullptr) return SVLLM_ERR_CUDA;
+  return run_lm_head_argmax(hidden, num_rows, hidden_size, hidden_stride, weight, vocab,
+                            weight_stride, out_ids, logits, logits_stride,
+                            static_cast<uint64_t*>(workspace), device, err,
+                            reinterpret_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -579,54 +611,29 @@ extern "C" int svllm_lm_head_argmax_static_bf16(const void* hidden, int64_t num_
                                                 void* logits, int64_t logits_stride,
                                                 svllm_stream stream) {
   using namespace svllm::k;
-  if (num_rows < 0 || hidden_size <= 0 || vocab <= 0 || hidden_stride < hidden_size ||
-      weight_stride < hidden_size || vocab >= (int64_t{1} << 31) ||
-      (logits != nullptr && logits_stride < vocab)) {
-    return SVLLM_ERR_INVALID_ARGUMENT;
-  }
+  int status = check_lm_head_sizes(num_rows, hidden_size, hidden_stride, vocab, weight_stride,
+                                   logits, logits_stride);
+  if (status != SVLLM_OK) return status;
   if (num_rows > kStaticScratchRows) return SVLLM_ERR_TOO_LARGE;
   if (num_rows == 0) return SVLLM_OK;
-  if (hidden == nullptr || weight == nullptr || out_ids == nullptr) {
-    return SVLLM_ERR_INVALID_ARGUMENT;
-  }
-  if (!aligned16(hidden) || !aligned16(weight) || (hidden_stride * 2) % 16 != 0 ||
-      (weight_stride * 2) % 16 != 0) {
-    return SVLLM_ERR_UNSUPPORTED;
-  }
+  status = check_lm_head_operands(hidden, hidden_stride, weight, weight_stride, out_ids);
+  if (status != SVLLM_OK) return status;
   int device;
   if (current_device(&device) != SVLLM_OK) return SVLLM_ERR_CUDA;
   int* err = library_error_word(device);
   uint64_t* keys = static_keys(device);  // the first call on a device looks it up
   if (err == nullptr || keys == nullptr) return SVLLM_ERR_CUDA;
   const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // the rows this call uses start at zero, whatever an earlier call left behind
+  // The finish kernel leaves every key it read at zero, so after a completed call the rows are
+  // clear already. This clear is for the cases where they are not: an earlier call whose kernels
+  // stopped early (a wait that timed out) or that overlapped this one on another stream. In a
+  // captured decode graph it is one memset node per step, ahead of the GEMM, and it keeps the
+  // GEMM from being scheduled early behind the kernel before it.
   if (cudaMemsetAsync(keys, 0, static_cast<size_t>(num_rows) * sizeof(uint64_t), s) !=
       cudaSuccess) {
     cudaGetLastError();
     return SVLLM_ERR_CUDA;
   }
-
-  LmHeadArgs a{};
-  a.m = num_rows;
-  a.n = vocab;
-  a.k = hidden_size;
-  a.keys = keys;
-  a.logits = logits;
-  a.logits_stride = logits_stride;
-  a.err = err;
-  int status;
-  if (num_rows <= kSwapMaxRows) {
-    status = launch_swap(hidden, hidden_stride, weight, weight_stride, a, device, s);
-  } else switch (pick_bn(num_rows, vocab, sm_count(device))) {
-    case 256: status = launch_gemm<256>(hidden, hidden_stride, weight, weight_stride, a, device, s); break;
-    case 224: status = launch_gemm<224>(hidden, hidden_stride, weight, weight_stride, a, device, s); break;
-    case 208: status = launch_gemm<208>(hidden, hidden_stride, weight, weight_stride, a, device, s); break;
-    case 192: status = launch_gemm<192>(hidden, hidden_stride, weight, weight_stride, a, device, s); break;
-    case 160: status = launch_gemm<160>(hidden, hidden_stride, weight, weight_stride, a, device, s); break;
-    default: status = launch_gemm<128>(hidden, hidden_stride, weight, weight_stride, a, device, s); break;
-  }
-  if (status != SVLLM_OK) return status;
-  const int64_t blocks = (num_rows + 255) / 256;
-  return launch(lm_head_argmax_finish_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s,
-                1, keys, num_rows, out_ids);
+  return run_lm_head_argmax(hidden, num_rows, hidden_size, hidden_stride, weight, vocab,
+                            weight_stride, out_ids, logits, logits_stride, keys, device, err, s);
 }

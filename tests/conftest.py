@@ -115,6 +115,21 @@ def assert_bf16_within_ulp(actual, expected, max_ulp: int, what: str = "") -> fl
     return float((d == 0).mean())
 
 
+def rope_within_rounding(out, ref, pre) -> np.ndarray:
+    """Per element: a rotated bf16 output within one bf16 rounding of each rotation term of the
+    reference (2^-7 of |x_i| + |x_{i+d/2}| of the pre-rotation values `pre`) plus one rounding of
+    the result (2^-8 of |ref|). The rotation cancels, so a result near zero can be many of its
+    own ulps off and still this close; the CPU oracle's cosf/sinf are the C library's, not
+    CUDA's. Arguments: bf16 bit patterns (or tensors) with the head dimension last."""
+    o = bf16_values(out).astype(np.float64)
+    r = bf16_values(ref).astype(np.float64)
+    p = bf16_values(pre).astype(np.float64)
+    half = p.shape[-1] // 2
+    mag = np.abs(p[..., :half]) + np.abs(p[..., half:])
+    mag = np.concatenate([mag, mag], axis=-1)
+    return np.abs(o - r) <= 2.0 ** -7 * mag + 2.0 ** -8 * np.abs(r) + 1e-30
+
+
 def assert_rel_f32(actual, expected, rtol: float = 1e-5, what: str = "", scale=None) -> None:
     """fp32: |a - e| <= rtol * max(|e|, s) per element (the fp32 ops' 1e-5 relative bar),
     where s is the magnitude the element was computed from: by default the RMS of its row (the

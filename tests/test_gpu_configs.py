@@ -24,7 +24,7 @@ import torch.nn.functional as F
 import oracle
 import svllm_capi as capi
 import svllm_ops
-from conftest import assert_bf16_within_ulp, assert_rel_f32, to_bits
+from conftest import assert_bf16_within_ulp, assert_rel_f32, rope_within_rounding, to_bits
 
 pytestmark = pytest.mark.gpu
 
@@ -121,6 +121,14 @@ def check_chain_bf16(inp, cfg, qk_norm=True, scaling=None, sample_rows=512):
                                      eps, invn)
     else:
         oq, ok = oracle.rope(host["q"], host["k"], host["pos"], invn)
+    # every sampled element within one rounding of each rotation term, and > 99% bit-exact
+    if qk_norm:
+        pre_q = oracle.rms_norm(host["q"].reshape(-1, d), host["qw"], eps).reshape(host["q"].shape)
+        pre_k = oracle.rms_norm(host["k"].reshape(-1, d), host["kw"], eps).reshape(host["k"].shape)
+    else:
+        pre_q, pre_k = host["q"], host["k"]
+    assert rope_within_rounding(to_bits(inp["q"][rows]), oq, pre_q).all()
+    assert rope_within_rounding(to_bits(inp["k"][rows]), ok, pre_k).all()
     assert (to_bits(inp["q"][rows]) == oq).mean() > 0.99
     assert (to_bits(inp["k"][rows]) == ok).mean() > 0.99
     oy = oracle.silu_and_mul(host["gate"], host["up"])

@@ -10,7 +10,7 @@ import torch
 
 import oracle
 import svllm_capi as capi
-from conftest import assert_bf16_within_ulp, random_t, to_bits
+from conftest import assert_bf16_within_ulp, random_t, rope_within_rounding, to_bits
 
 pytestmark = pytest.mark.gpu
 
@@ -58,7 +58,12 @@ def test_single_token(cuda, op):
         inv = oracle.inv_freq(1e6, 128)
         oq, ok = oracle.qk_norm_rope(to_bits(q), to_bits(k), to_bits(qw), to_bits(kw),
                                      pos.cpu().numpy(), 1e-6, inv)
+        pre_q = oracle.rms_norm(to_bits(q).reshape(-1, 128), to_bits(qw), 1e-6).reshape(16, 128)
+        pre_k = oracle.rms_norm(to_bits(k).reshape(-1, 128), to_bits(kw), 1e-6).reshape(8, 128)
         capi.qk_norm_rope(q, k, qw, kw, pos, 1e-6, inv)
+        # every element within one rounding of each rotation term of the oracle, > 98% exact
+        assert rope_within_rounding(to_bits(q)[0], oq[0], pre_q).all()
+        assert rope_within_rounding(to_bits(k)[0], ok[0], pre_k).all()
         assert (to_bits(q) == oq).mean() > 0.98 and (to_bits(k) == ok).mean() > 0.98
     elif op == "silu_and_mul":
         g, u = random_t(1, 3072, device=cuda, seed=9), random_t(1, 3072, device=cuda, seed=10)

@@ -33,6 +33,17 @@ def run(hidden, weight, with_logits=True):
 
 def check(hidden, weight):
     ids, logits = run(hidden, weight)
+    # against the exact product in fp32: each logit is the fp32 sum rounded once to bf16, so it
+    # is within one bf16 ulp of the fp32 value plus the fp32 accumulation's own error
+    # (K * 2^-24 of the sum of |terms|, K = hidden size)
+    h32, w32 = hidden.float(), weight.float()
+    exact = torch.matmul(h32, w32.t())
+    terms = torch.matmul(h32.abs(), w32.abs().t())
+    bound = 2.0 ** -8 * exact.abs() + hidden.shape[1] * 2.0 ** -24 * terms
+    assert bool(((logits.float() - exact).abs() <= bound).all()), "logits vs the fp32 product"
+    top2 = exact.topk(2, dim=-1).values
+    clear32 = (top2[:, 0] - top2[:, 1]) > 2 * bound.max(dim=-1).values
+    assert torch.equal(ids[clear32], torch.argmax(exact, dim=-1)[clear32]), "ids vs fp32 argmax"
     ref = torch.matmul(hidden, weight.t())
     exact = assert_bf16_within_ulp(logits, ref, 1, "logits vs cuBLAS")
     assert exact > 0.99, f"only {exact:.4%} of the logits identical to cuBLAS's"

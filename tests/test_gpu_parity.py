@@ -27,7 +27,7 @@ import torch.nn.functional as F
 import oracle
 import svllm_capi as capi
 from conftest import (assert_bf16_within_ulp, assert_rel_f32, bf16_values, from_bits, random_t,
-                      to_bits)
+                      rope_within_rounding, to_bits)
 
 pytestmark = pytest.mark.gpu
 
@@ -122,15 +122,7 @@ def test_add_rms_norm(cuda, dt, shape):
 # ---------------------------------------------------------------------------------------------
 # rotary embedding
 
-def rope_bound_ok(out, ref, pre) -> np.ndarray:
-    """Within one bf16 rounding of each rotation term, plus one of the result."""
-    o = bf16_values(out).astype(np.float64)
-    r = bf16_values(ref).astype(np.float64)
-    p = bf16_values(pre).astype(np.float64)
-    half = p.shape[-1] // 2
-    mag = np.abs(p[..., :half]) + np.abs(p[..., half:])
-    mag = np.concatenate([mag, mag], axis=-1)
-    return np.abs(o - r) <= 2.0 ** -7 * mag + 2.0 ** -8 * np.abs(r) + 1e-30
+rope_bound_ok = rope_within_rounding
 
 
 def torch_rope(x, pos, inv):
@@ -468,6 +460,14 @@ def test_rope_cache(cuda, dt, with_norm, hq, hk, d):
     mask[s_w] = False
     assert not flat_k[mask].any() and not flat_v[mask].any(), "a slot not in slot_mapping changed"
     if dt == torch.bfloat16:
+        # every element within one rounding of each rotation term, and > 99% bit-exact
+        if with_norm:
+            pre_q = oracle.rms_norm(qn.reshape(-1, d), np_of(qw), 1e-6).reshape(qn.shape)
+            pre_k = oracle.rms_norm(kn.reshape(-1, d), np_of(kw), 1e-6).reshape(kn.shape)
+        else:
+            pre_q, pre_k = qn, kn
+        assert rope_bound_ok(np_of(q.contiguous()), rq, pre_q).all()
+        assert rope_bound_ok(np_of(k.contiguous()), rk, pre_k).all()
         assert (np_of(q.contiguous()) == rq).mean() > 0.99
         assert (np_of(k.contiguous()) == rk).mean() > 0.99
     else:

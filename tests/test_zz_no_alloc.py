@@ -30,24 +30,28 @@ def static_call(ids, hidden, weight, logits=None) -> int:
         logits.stride(0) if logits is not None else 0, ctypes.c_void_p(stream))
 
 
+@pytest.mark.parametrize("with_logits", [True, False], ids=["ids+logits", "ids-only"])
 @pytest.mark.parametrize("rows", [7, 300])  # both orientations of the kernel
-def test_matches_the_workspace_entry_point_on_two_calls(cuda, rows):
+def test_matches_the_workspace_entry_point_on_two_calls(cuda, rows, with_logits):
+    """Two calls in a row on different inputs; ids-only is the decode use (no logits kept)."""
     vocab, hidden_size = 20000, 1024
     for call in range(2):
-        g = torch.Generator(device=cuda).manual_seed(100 * rows + call)
+        g = torch.Generator(device=cuda).manual_seed(100 * rows + call + (7 if with_logits else 0))
         hidden = torch.randn(rows, hidden_size, device=cuda, generator=g).bfloat16()
         weight = (torch.randn(vocab, hidden_size, device=cuda, generator=g) * 0.05).bfloat16()
         ids = torch.empty(rows, dtype=torch.int64, device=cuda)
-        logits = torch.empty(rows, vocab, dtype=torch.bfloat16, device=cuda)
+        logits = (torch.empty(rows, vocab, dtype=torch.bfloat16, device=cuda) if with_logits
+                  else None)
         assert static_call(ids, hidden, weight, logits) == 0
         want_ids = torch.empty_like(ids)
-        want_logits = torch.empty_like(logits)
+        want_logits = torch.empty_like(logits) if with_logits else None
         workspace = torch.zeros(rows, dtype=torch.int64, device=cuda)
         capi.lm_head_argmax(want_ids, hidden, weight, workspace, want_logits)
         torch.cuda.synchronize()
         assert torch.equal(ids, want_ids), f"call {call}"
-        assert torch.equal(logits, want_logits), f"call {call}"
-        assert torch.equal(ids, torch.argmax(logits, dim=-1))
+        if with_logits:
+            assert torch.equal(logits, want_logits), f"call {call}"
+            assert torch.equal(ids, torch.argmax(logits, dim=-1))
 
 
 def test_rejects_more_rows_than_the_scratch_holds(cuda):
