@@ -276,7 +276,8 @@ int launch_embedding(void* out, const void* ids, int id_type, const void* table,
                                        threads, smem, device);
       if (per_sm > 0) {
         const int64_t grid = persistent_grid((num_tokens + warps - 1) / warps, device, per_sm);
-        return launch(embedding_bulk_kernel, dim3(static_cast<unsigned>(grid)), dim3(threads),
+        return launch_streaming(num_tokens * static_cast<int64_t>(a.row_bytes) * 2,
+                                embedding_bulk_kernel, dim3(static_cast<unsigned>(grid)), dim3(threads),
                       smem, stream, 1, a);
       }
     }

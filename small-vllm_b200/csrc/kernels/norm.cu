@@ -394,7 +394,8 @@ int launch_norm(void* out, const void* x, void* residual, const void* weight, in
         if (per_sm > 0) {
           const int64_t num_units = (num_rows + rows - 1) / rows;
           const int64_t grid = persistent_grid((num_units + warps - 1) / warps, device, per_sm);
-          return launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1,
+          return launch_streaming(num_rows * row_bytes * (kAdd ? 4 : 2), kernel,
+                                  dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1,
                         a);
         }
       }

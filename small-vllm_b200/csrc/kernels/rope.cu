@@ -600,7 +600,8 @@ int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
       const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(kernel), threads, smem, device);
       if (per_sm > 0) {
         const int64_t grid = persistent_grid((num_tokens + warps - 1) / warps, device, per_sm);
-        return launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1,
+        return launch_streaming(num_tokens * (2 * (q_bytes + k_bytes) + 3 * v_bytes), kernel,
+                                dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1,
                       a);
       }
     }

@@ -348,8 +348,9 @@ int launch_silu(void* out, const void* gate, const void* up, int64_t num_rows, i
       if (per_sm > 0) {
         const int64_t units = a.rows * ((a.cols + chunk - 1) / chunk);
         const int64_t grid = persistent_grid((units + warps - 1) / warps, device, per_sm);
-        return launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1,
-                      a);
+        return launch_streaming(a.rows * a.cols * static_cast<int64_t>(sizeof(S)) * 3, kernel,
+                                dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1,
+                                a);
       }
     }
   }
