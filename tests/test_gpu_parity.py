@@ -286,10 +286,12 @@ def test_embedding_bad_ids_zero_rows_and_raise_the_error_word(cuda):
     assert capi.read_device_error(0, reset=True) & capi.DEVERR_BAD_INDEX
 
 
-# Batches with at least one token per table row take the vocabulary-bucket walk (the gather
+# Batches with at least half a token per table row take the vocabulary-bucket walk (the gather
 # visits its tokens once per L2-sized slice of the table); these tables span 2 to 24 slices.
 @pytest.mark.parametrize("vocab, hidden, T, dt, ids_dtype", [
     (8192, 1024, 16384, torch.bfloat16, torch.int32),
+    (8192, 1024, 4096, torch.bfloat16, torch.int64),  # half a token per row
+    (151936, 1024, 131072, torch.bfloat16, torch.int32),  # one rank's share of the 1M sweep
     (20000, 2048, 40000, torch.bfloat16, torch.int64),
     (4096, 1024, 9000, torch.float32, torch.int32),
     (151936, 1024, 300000, torch.bfloat16, torch.int32),
