@@ -152,7 +152,7 @@ def parse_args():
     p.add_argument("--no-configs", action="store_true",
                    help="skip the benchmark definition's configs 0-3 (measured at N=1 beside "
                         "the sweep)")
-    p.add_argument("--cpu-sample-tokens", type=int, default=32768,
+    p.add_argument("--cpu-sample-tokens", type=int, default=131072,
                    help="token rows of the cpu_baseline sample in the GPU arm's line")
     p.add_argument("--reference-tokens", type=int, default=0,
                    help="--impl reference: token rows per timed pass (default: the workload's "
@@ -1232,7 +1232,7 @@ def main() -> int:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_chain_sample(min(args.cpu_sample_tokens, total), cfg, pos_spec, 2,
-                               min_seconds=5.0)
+                               min_seconds=10.0)
 
     configs = None
     if rank == 0 and world == 1 and args.workload == "sweep" and not args.no_configs:
