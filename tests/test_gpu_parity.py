@@ -397,6 +397,14 @@ def test_pipeline_shape_does_not_change_results(cuda, unit, stages, warps):
     assert pipeline_digest(spec) == pipeline_digest(None)
 
 
+def test_malformed_pipeline_entries_are_ignored(cuda):
+    """Entries that do not parse, name no op, or are out of range leave the defaults in force;
+    a valid entry beside them still applies (results are the same either way)."""
+    spec = ("rms_norm=abc,no_such_op=4096:2:8,silu_and_mul=100:2:8,rope=4096:99:8,"
+            "embedding=4096:1:8,add_rms_norm,=,embedding=0:3:4")
+    assert pipeline_digest(spec) == pipeline_digest(None)
+
+
 def test_silu_table_path_is_exhaustively_identical(cuda):
     """Every one of the 65536 bf16 gate patterns (NaNs and infinities included) through the
     table path (a batch large enough to take it) and through the direct path (one row, too small
