@@ -49,7 +49,7 @@ typedef enum svllm_status {
   SVLLM_OK = 0,
   SVLLM_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad size, stride or dtype */
   SVLLM_ERR_TOO_LARGE = 2,        /* sizes exceed the kernel's index range */
-  SVLLM_ERR_UNSUPPORTED = 3,      /* a shape this build has no kernel for */
+  SVLLM_ERR_UNSUPPORTED = 3,      /* a shape the library has no kernel for */
   SVLLM_ERR_LAUNCH = 4,           /* the kernel launch failed */
   SVLLM_ERR_CUDA = 5              /* another CUDA runtime call failed */
 } svllm_status;

@@ -10,7 +10,7 @@
 3. oracle/_ref/reference_tests/: the reference's own Python tests of the op API, unmodified
    (tests/python/conftest.py, test_rms_norm.py, test_bindings.py, and the pyproject.toml whose
    version test_bindings.py checks), copied in the reference's layout so that they run against
-   this build's svllm_ops with SVLLM_BUILD_DIR pointing at it (tests/test_reference_suite.py).
+   small-vllm_b200's svllm_ops with SVLLM_BUILD_DIR pointing at it (tests/test_reference_suite.py).
 
 The reference checkout is given by --reference or the SVLLM_REFERENCE environment variable;
 without either, only the restatement is built.

@@ -1,10 +1,10 @@
-"""The reference's own op-API tests, run unmodified against this build's svllm_ops.
+"""The reference's own op-API tests, run unmodified against small-vllm_b200's svllm_ops.
 
 small-vLLM's tests/python/conftest.py, test_rms_norm.py and test_bindings.py (with the
 pyproject.toml whose version test_bindings.py checks) are copied byte for byte by oracle/build.py
 into oracle/_ref/reference_tests/, in the reference's own layout, and run here in a fresh
 interpreter with SVLLM_BUILD_DIR pointing at small-vllm_b200/ (the reference's conftest.py:10-13
-puts $SVLLM_BUILD_DIR/python on sys.path, where this build's svllm_ops lives). The CPU run hides
+puts $SVLLM_BUILD_DIR/python on sys.path, where small-vllm_b200's svllm_ops lives). The CPU run hides
 the GPU, so the reference's CUDA cases skip as they do on a CPU machine; the GPU run needs every
 case, CUDA included, to pass. tests/test_cmake_build.py runs the same suite against the module
 that the CMake target builds.
