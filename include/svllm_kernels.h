@@ -21,6 +21,12 @@
  *     CPU path behind these functions.
  *   - `err` (optional, may be NULL) is a device int the kernel ORs SVLLM_DEVERR_* bits into.
  *     With NULL the library's own per-device word is used; svllm_read_device_error reads it.
+ *   - No launch setting can be changed through this ABI: each op's pipeline shape (bytes per
+ *     stage, stages, warps per CTA) is a tuned constant. For tuning sweeps the environment
+ *     variable SVLLM_PIPELINE="op=unit_bytes:stages:warps[,...]" (op: rms_norm, add_rms_norm,
+ *     qk_norm_rope, rope, silu_and_mul, embedding; 0 keeps a value) is read once, at the
+ *     process's first launch; entries that do not parse are ignored. Results do not depend on
+ *     the shape.
  *
  * Reference interfaces these replace or extend (small-vLLM, paths within its project):
  *   src/ops/rms_norm.h:13            at::Tensor svllm::ops::rms_norm(x, weight, eps)
