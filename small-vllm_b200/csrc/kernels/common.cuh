@@ -209,12 +209,23 @@ __device__ __forceinline__ uint4 ld_shared_v4(const void* p) {
 // mbarrier + bulk copy (cp.async.bulk, the non-tensor TMA path). No copy in this library is
 // broadcast to other CTAs of a cluster: every copy moves this GPU's own memory into its own CTA.
 
-// Programmatic dependent launch: wait until the kernel before this one in the stream has
-// completed and its memory is visible (a no-op when launched without the attribute), then let
-// the next kernel be scheduled. Every kernel runs this first, before any memory access.
-__device__ __forceinline__ void grid_dependency_sync() {
+// Programmatic dependent launch, in two halves. grid_dependency_wait: wait until the kernel
+// before this one in the stream has completed and its memory is visible (a no-op when launched
+// without the attribute); every kernel runs it first, before any memory access.
+// allow_dependents: let the next kernel in the stream be scheduled now, while this one runs; a
+// kernel that never calls it lets the next one be scheduled as its CTAs exit.
+__device__ __forceinline__ void grid_dependency_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void allow_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Both, for kernels that always let the next one be scheduled at their start.
+__device__ __forceinline__ void grid_dependency_sync() {
+  grid_dependency_wait();
+  allow_dependents();
 }
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {

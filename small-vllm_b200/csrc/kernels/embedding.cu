@@ -48,6 +48,7 @@ struct EmbArgs {
   int stage_bytes;
   int ring_offset;       // after the mbarriers and the per-stage token slots
   int passes;            // vocabulary buckets, one per pass over the warp's tokens
+  int early_dependents;  // let the next kernel be scheduled at this one's start
   int64_t bucket_rows;   // rows per bucket: ceil(vocab / passes)
 };
 
@@ -57,7 +58,8 @@ __device__ __forceinline__ int64_t load_id(const void* ids, int is_i64, int64_t 
 }
 
 __global__ void __launch_bounds__(512) embedding_bulk_kernel(const EmbArgs a) {
-  grid_dependency_sync();
+  grid_dependency_wait();
+  if (a.early_dependents) allow_dependents();
   extern __shared__ __align__(128) uint8_t smem[];
   const int warps = blockDim.x / kWarpSize;
   const int warp = threadIdx.x / kWarpSize;
@@ -277,8 +279,8 @@ int launch_embedding(void* out, const void* ids, int id_type, const void* table,
                                        threads, smem, device);
       if (per_sm > 0) {
         const int64_t grid = persistent_grid((num_tokens + warps - 1) / warps, device, per_sm);
-        return launch_streaming(num_tokens * static_cast<int64_t>(a.row_bytes) * 2,
-                                embedding_bulk_kernel, dim3(static_cast<unsigned>(grid)), dim3(threads),
+        a.early_dependents = early_dependents(num_tokens * static_cast<int64_t>(a.row_bytes) * 2);
+        return launch(embedding_bulk_kernel, dim3(static_cast<unsigned>(grid)), dim3(threads),
                       smem, stream, 1, a);
       }
     }

@@ -103,22 +103,18 @@ int launch(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaSt
                      std::forward<Args>(args)...);
 }
 
-// Streaming kernels that move at least this many bytes are launched without programmatic
-// dependent launch. Early scheduling hides the gap between kernels (a few microseconds): worth it
-// for decode- and prefill-sized launches, and measured to cost time for long ones. On a B200,
-// eager launches: the 1M-token chain (embedding, add_rms_norm, qk_norm_rope, silu_and_mul, 4-19 GB
-// each) ran at 6497 GB/s with early scheduling and 6675 without; the 16384-token Llama chain
-// (0.13-0.8 GB per op) at 5939 with and 5837 without. From a CUDA graph both were within 1%.
-constexpr int64_t kEarlyLaunchMaxBytes = int64_t{1} << 30;
+// The streaming kernels let the next kernel in the stream be scheduled at their start only when
+// they move less than this many bytes; a larger launch lets it be scheduled as its CTAs exit.
+// Scheduling the next kernel at the start hides its launch and start-up behind this one: it pays
+// for decode-sized launches (the Qwen3-0.6B decode step at batch 1: 0.89 ms against 1.06 ms with
+// the exit point), and costs time behind long ones (the 1M-token chain launched eagerly ran at
+// 6545 GB/s with every kernel triggering at its start, 6721 with the exit point). Measured on a
+// B200 against no early scheduling at all for launches of 1 GB or more: the 131k-token chain
+// 6437 -> 6505 GB/s, the 73k-token prefill chain 6291 -> 6343, the 1M and 16k (Llama) chains and
+// the decode step unchanged.
+constexpr int64_t kEarlyDependentsMaxBytes = int64_t{64} << 20;
 
-// `launch` for a streaming kernel that moves `bytes` of HBM traffic: scheduled early below
-// kEarlyLaunchMaxBytes, after the kernel before it has completed at or above.
-template <class... Params, class... Args>
-int launch_streaming(int64_t bytes, void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
-                     cudaStream_t stream, unsigned cluster, Args&&... args) {
-  return launch_with(bytes < kEarlyLaunchMaxBytes, kernel, grid, block, smem, stream, cluster,
-                     std::forward<Args>(args)...);
-}
+inline int early_dependents(int64_t bytes) { return bytes < kEarlyDependentsMaxBytes ? 1 : 0; }
 
 // As `launch`, but the grid starts only once the kernel before it has completed. For grids
 // whose CTAs are heavy enough (all of an SM's registers in four CTAs) that scheduling them early

@@ -52,6 +52,7 @@ struct NormArgs {
   float eps;
   int* err;
   // bulk-copy path
+  int early_dependents;  // let the next kernel be scheduled at this one's start
   int rows_per_unit;     // R
   int interleave;        // unit order (WarpUnits)
   float inv_hidden;      // 1 / hidden when hidden is a power of two, else 0
@@ -77,7 +78,8 @@ __device__ __forceinline__ void load_rows(uint8_t* dst, const void* base, int64_
 
 template <class E, int G, int V, bool kAdd>
 __global__ void __launch_bounds__(512) norm_bulk_kernel(const NormArgs a) {
-  grid_dependency_sync();
+  grid_dependency_wait();
+  if (a.early_dependents) allow_dependents();
   using S = typename E::Storage;
   constexpr int kVec = E::kPerVec;
   constexpr int kRowsPerPass = kWarpSize / G;
@@ -394,8 +396,8 @@ int launch_norm(void* out, const void* x, void* residual, const void* weight, in
         if (per_sm > 0) {
           const int64_t num_units = (num_rows + rows - 1) / rows;
           const int64_t grid = persistent_grid((num_units + warps - 1) / warps, device, per_sm);
-          return launch_streaming(num_rows * row_bytes * (kAdd ? 4 : 2), kernel,
-                                  dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1,
+          a.early_dependents = early_dependents(num_rows * row_bytes * (kAdd ? 4 : 2));
+          return launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1,
                         a);
         }
       }

@@ -56,6 +56,7 @@ struct RopeArgs {
   int pos_is_i64;
   int norm_vec;  // plain path: the reference would load 8-element vectors
   int interleave;  // token order (WarpUnits)
+  int early_dependents;  // let the next kernel be scheduled at this one's start
   float eps;
   int* err;
   // cache variants
@@ -160,7 +161,8 @@ constexpr int kVRegs = 4;
 // kPasses == 0: a runtime loop over any number of heads.
 template <class E, int G, bool kNorm, bool kCache, int kPasses>
 __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ RopeArgs a) {
-  grid_dependency_sync();
+  grid_dependency_wait();
+  if (a.early_dependents) allow_dependents();
   using S = typename E::Storage;
   constexpr int kVec = E::kPerVec;
   constexpr int kHalf = kVec * G;  // head_dim / 2
@@ -600,8 +602,8 @@ int launch_rope(void* q, void* k, const void* q_weight, const void* k_weight,
       const int per_sm = blocks_per_sm(reinterpret_cast<const void*>(kernel), threads, smem, device);
       if (per_sm > 0) {
         const int64_t grid = persistent_grid((num_tokens + warps - 1) / warps, device, per_sm);
-        return launch_streaming(num_tokens * (2 * (q_bytes + k_bytes) + 3 * v_bytes), kernel,
-                                dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1,
+        a.early_dependents = early_dependents(num_tokens * (2 * (q_bytes + k_bytes) + 3 * v_bytes));
+        return launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1,
                       a);
       }
     }

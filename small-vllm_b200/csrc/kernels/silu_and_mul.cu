@@ -48,6 +48,7 @@ struct SiluArgs {
   int stage_bytes;       // gate chunk, then up chunk
   int table_offset;      // table path: byte offset of the 65536-entry table
   int interleave;        // unit order (WarpUnits)
+  int early_dependents;  // let the next kernel be scheduled at this one's start
   int ring_offset;
 };
 
@@ -137,7 +138,8 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
 
 template <class E, bool kTable>
 __global__ void __launch_bounds__(512) silu_bulk_kernel(const SiluArgs a) {
-  grid_dependency_sync();
+  grid_dependency_wait();
+  if (a.early_dependents) allow_dependents();
   using S = typename E::Storage;
   constexpr int kVec = E::kPerVec;
   static_assert(!kTable || sizeof(S) == 2, "the table path is for bf16");
@@ -348,9 +350,8 @@ int launch_silu(void* out, const void* gate, const void* up, int64_t num_rows, i
       if (per_sm > 0) {
         const int64_t units = a.rows * ((a.cols + chunk - 1) / chunk);
         const int64_t grid = persistent_grid((units + warps - 1) / warps, device, per_sm);
-        return launch_streaming(a.rows * a.cols * static_cast<int64_t>(sizeof(S)) * 3, kernel,
-                                dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1,
-                                a);
+        a.early_dependents = early_dependents(a.rows * a.cols * static_cast<int64_t>(sizeof(S)) * 3);
+        return launch(kernel, dim3(static_cast<unsigned>(grid)), dim3(threads), smem, stream, 1, a);
       }
     }
   }
