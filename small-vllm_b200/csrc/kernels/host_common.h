@@ -106,8 +106,8 @@ int launch(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaSt
 // The streaming kernels let the next kernel in the stream be scheduled at their start only when
 // they move less than this many bytes; a larger launch lets it be scheduled as its CTAs exit.
 // Scheduling the next kernel at the start hides its launch and start-up behind this one: it pays
-// for decode-sized launches (the Qwen3-0.6B decode step at batch 1: 0.89 ms against 1.06 ms with
-// the exit point), and costs time behind long ones (the 1M-token chain launched eagerly ran at
+// for decode-sized launches (the Qwen3-0.6B decode step at batch 1, one box: 0.94 ms against
+// 1.06 ms with the exit point), and costs time behind long ones (the 1M-token chain launched eagerly ran at
 // 6545 GB/s with every kernel triggering at its start, 6721 with the exit point). Measured on a
 // B200 against no early scheduling at all for launches of 1 GB or more: the 131k-token chain
 // 6437 -> 6505 GB/s, the 73k-token prefill chain 6291 -> 6343, the 1M and 16k (Llama) chains and
