@@ -24,9 +24,9 @@
  *   - No launch setting can be changed through this ABI: each op's pipeline shape (bytes per
  *     stage, stages, warps per CTA) is a tuned constant. For tuning sweeps the environment
  *     variable SVLLM_PIPELINE="op=unit_bytes:stages:warps[,...]" (op: rms_norm, add_rms_norm,
- *     qk_norm_rope, rope, silu_and_mul, embedding; 0 keeps a value) is read once, at the
- *     process's first launch; entries that do not parse are ignored. Results do not depend on
- *     the shape.
+ *     qk_norm_rope, rope, silu_and_mul, embedding; unit_bytes a multiple of 16, stages 2-16,
+ *     warps 1-16; 0 keeps a value) is read once, at the process's first launch; entries that
+ *     do not parse or are out of range are ignored. Results do not depend on the shape.
  *
  * Reference interfaces these replace or extend (small-vLLM, paths within its project):
  *   src/ops/rms_norm.h:13            at::Tensor svllm::ops::rms_norm(x, weight, eps)

@@ -89,7 +89,7 @@ const PipelineShape* shapes_in_force() {
       long long unit = -1, stages = -1, warps = -1;
       if (std::sscanf(item.c_str() + eq + 1, "%lld:%lld:%lld", &unit, &stages, &warps) != 3 ||
           unit < 0 || stages < 0 || warps < 0 || unit > (1 << 20) || unit % 16 != 0 ||
-          stages > 16 || warps > 32 || (stages != 0 && stages < 2)) {
+          stages > 16 || warps > kMaxBulkWarps || (stages != 0 && stages < 2)) {
         continue;
       }
       for (int i = 0; i < static_cast<int>(OpId::kCount); ++i) {

@@ -39,6 +39,10 @@ int blocks_per_sm(const void* func, int threads, size_t smem_bytes, int device);
 // Largest dynamic shared memory a CTA may use on this architecture.
 constexpr size_t kMaxSmemPerCta = 227 * 1024;
 
+// Most warps a streaming (bulk-copy) kernel's CTA may have: those kernels are compiled with
+// __launch_bounds__(512).
+constexpr int kMaxBulkWarps = 16;
+
 // The library's own error word on `device` (a __device__ int, address cached per device).
 int* library_error_word(int device);
 

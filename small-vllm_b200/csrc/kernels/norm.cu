@@ -365,7 +365,8 @@ int launch_norm(void* out, const void* x, void* residual, const void* weight, in
       // Short rows (at most 256 bf16) spend more instructions per byte on their reductions and
       // take half again as many warps (rms_norm at 16M rows of 128 on a B200: 5088 -> 6551
       // GB/s with 12 warps instead of 8).
-      const int tuned_warps = !kAdd && row_bytes <= 512 ? shape.warps * 3 / 2 : shape.warps;
+      const int tuned_warps =
+          std::min(kMaxBulkWarps, !kAdd && row_bytes <= 512 ? shape.warps * 3 / 2 : shape.warps);
       int64_t rows = std::max<int64_t>(1, shape.unit_bytes / unit_row_bytes);
       rows = std::max<int64_t>(rows_per_pass, rows / rows_per_pass * rows_per_pass);
       rows = std::min<int64_t>(rows, round_up(num_rows, rows_per_pass));

@@ -359,14 +359,18 @@ pos = torch.arange(5000, device=cuda) * 7
 inv = torch.tensor([1e6 ** (-2 * i / 128) for i in range(64)], dtype=torch.float32)
 table = random_t(4000, 1024, device=cuda, seed=30)
 ids = torch.randint(0, 4000, (9000,), generator=torch.Generator().manual_seed(31)).to(cuda)
+xs = random_t(40000, 128, device=cuda, seed=32)  # short rows: half again as many warps
+ws = random_t(128, device=cuda, seed=33)
 out, sout, eout = torch.empty_like(x), torch.empty_like(gate), torch.empty(9000, 1024, dtype=torch.bfloat16, device=cuda)
+souts = torch.empty_like(xs)
 capi.rms_norm(out, x, w, 1e-6)
+capi.rms_norm(souts, xs, ws, 1e-6)
 capi.silu_and_mul(sout, gate, up)
 capi.rope(q, k, pos, inv)
 capi.embedding(eout, ids, table)
 torch.cuda.synchronize()
 h = hashlib.sha256()
-for t in (out, sout, q, k, eout):
+for t in (out, souts, sout, q, k, eout):
     h.update(t.view(torch.int16).cpu().numpy().tobytes())
 print(h.hexdigest())
 """
@@ -390,7 +394,9 @@ def pipeline_digest(spec: str | None) -> str:
     return proc.stdout.strip().splitlines()[-1]
 
 
-@pytest.mark.parametrize("unit, stages, warps", [(2048, 2, 1), (4096, 3, 8), (16384, 4, 2)])
+# (4096, 2, 12): short rows take half again as many warps, capped at the kernels' 16
+@pytest.mark.parametrize("unit, stages, warps",
+                         [(2048, 2, 1), (4096, 3, 8), (16384, 4, 2), (4096, 2, 12)])
 def test_pipeline_shape_does_not_change_results(cuda, unit, stages, warps):
     spec = ",".join(f"{op}={unit}:{stages}:{warps}"
                     for op in ("rms_norm", "silu_and_mul", "rope", "embedding"))
@@ -401,7 +407,7 @@ def test_malformed_pipeline_entries_are_ignored(cuda):
     """Entries that do not parse, name no op, or are out of range leave the defaults in force;
     a valid entry beside them still applies (results are the same either way)."""
     spec = ("rms_norm=abc,no_such_op=4096:2:8,silu_and_mul=100:2:8,rope=4096:99:8,"
-            "embedding=4096:1:8,add_rms_norm,=,embedding=0:3:4")
+            "embedding=4096:1:8,rms_norm=4096:2:17,add_rms_norm,=,embedding=0:3:4")
     assert pipeline_digest(spec) == pipeline_digest(None)
 
 
