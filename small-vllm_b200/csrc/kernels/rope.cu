@@ -32,6 +32,7 @@
 #include <cstdint>
 #include <cmath>
 #include <cstring>
+#include <type_traits>
 
 #include "common.cuh"
 #include "host_common.h"
@@ -290,10 +291,23 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
         unpack<E>(lo, lf);
         unpack<E>(hi, hf);
         float p_lo = 0.0f, p_hi = 0.0f;
+        // bf16: element e of each half as one fp32 pair, so the two running sums and the two
+        // scalings take one packed instruction per element (same roundings, same order)
+        uint64_t pair[kVec];
+        if constexpr (std::is_same_v<E, Bf16>) {
+          uint64_t acc = f32x2(0.0f, 0.0f);
 #pragma unroll
-        for (int e = 0; e < kVec; ++e) {
-          p_lo = __fmaf_rn(lf[e], lf[e], p_lo);
-          p_hi = __fmaf_rn(hf[e], hf[e], p_hi);
+          for (int e = 0; e < kVec; ++e) {
+            pair[e] = f32x2(lf[e], hf[e]);
+            acc = f32x2_fma(pair[e], pair[e], acc);
+          }
+          f32x2_split(acc, p_lo, p_hi);
+        } else {
+#pragma unroll
+          for (int e = 0; e < kVec; ++e) {
+            p_lo = __fmaf_rn(lf[e], lf[e], p_lo);
+            p_hi = __fmaf_rn(hf[e], hf[e], p_hi);
+          }
         }
         float total;
         if constexpr (2 * G <= kWarpSize) {
@@ -303,8 +317,26 @@ __global__ void __launch_bounds__(512) rope_bulk_kernel(const __grid_constant__ 
         }
         // sum / head_dim: head_dim is a power of two here, so the multiply is exact
         const float inv_rms = rsqrtf(__fadd_rn(__fmul_rn(total, 1.0f / kDim), a.eps));
-        lo = normalize_vec<E>(lo, inv_rms, is_q ? qw_lo : kw_lo);
-        hi = normalize_vec<E>(hi, inv_rms, is_q ? qw_hi : kw_hi);
+        if constexpr (std::is_same_v<E, Bf16>) {
+          // round(round(x * inv_rms) * w), as normalize_vec computes it
+          const uint64_t inv2 = f32x2(inv_rms, inv_rms);
+          float nl[kVec], nh[kVec];
+#pragma unroll
+          for (int e = 0; e < kVec; ++e) f32x2_split(f32x2_mul(pair[e], inv2), nl[e], nh[e]);
+          const uint4& wl = is_q ? qw_lo : kw_lo;
+          const uint4& wh = is_q ? qw_hi : kw_hi;
+          uint32_t rl[4], rh[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            rl[i] = bf16x2_mul(pack_bf16x2(nl[2 * i], nl[2 * i + 1]), word(wl, i));
+            rh[i] = bf16x2_mul(pack_bf16x2(nh[2 * i], nh[2 * i + 1]), word(wh, i));
+          }
+          lo = make_uint4(rl[0], rl[1], rl[2], rl[3]);
+          hi = make_uint4(rh[0], rh[1], rh[2], rh[3]);
+        } else {
+          lo = normalize_vec<E>(lo, inv_rms, is_q ? qw_lo : kw_lo);
+          hi = normalize_vec<E>(hi, inv_rms, is_q ? qw_hi : kw_hi);
+        }
       }
       trig.rotate(lo, hi);
       if (valid) {
