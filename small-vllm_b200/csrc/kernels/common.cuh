@@ -192,6 +192,23 @@ __device__ __forceinline__ uint4 normalize_vec<Bf16>(const uint4& h, float inv_r
                     bf16x2_mul(n[3], w.w));
 }
 
+// normalize_vec<Bf16> with the scaling by inv_rms as four packed fp32 multiplies (same results).
+__device__ __forceinline__ uint4 normalize_vec_packed(const uint4& h, float inv_rms,
+                                                      const uint4& w) {
+  float f[8];
+  unpack<Bf16>(h, f);
+  uint32_t n[4];
+  const uint64_t inv2 = f32x2(inv_rms, inv_rms);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float a, b;
+    f32x2_split(f32x2_mul(f32x2(f[2 * i], f[2 * i + 1]), inv2), a, b);
+    n[i] = pack_bf16x2(a, b);
+  }
+  return make_uint4(bf16x2_mul(n[0], w.x), bf16x2_mul(n[1], w.y), bf16x2_mul(n[2], w.z),
+                    bf16x2_mul(n[3], w.w));
+}
+
 template <>
 __device__ __forceinline__ uint4 normalize_vec<F32>(const uint4& h, float inv_rms,
                                                     const uint4& w) {

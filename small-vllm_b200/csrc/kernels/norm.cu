@@ -28,6 +28,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <cstdint>
 
 #include "common.cuh"
@@ -83,6 +84,12 @@ __global__ void __launch_bounds__(512) norm_bulk_kernel(const NormArgs a) {
   using S = typename E::Storage;
   constexpr int kVec = E::kPerVec;
   constexpr int kRowsPerPass = kWarpSize / G;
+  // Sums of squares and the scaling by 1/RMS in packed fp32 pairs (bit-identical). Measured on a
+  // B200 for plain bf16 rms_norm with an even number of vectors per lane: 1M x 1024 6220 -> 6560
+  // GB/s, 16384 x 2048 5890 -> 6300. With the residual add (1M x 1024: 6480 -> 5770) and for one
+  // vector per lane (16M x 128: 6410 -> 6040, the scaling alone packed) it was slower; those keep
+  // scalar fp32.
+  constexpr bool kPacked = std::is_same_v<E, Bf16> && V % 2 == 0 && !kAdd;
   extern __shared__ __align__(128) uint8_t smem[];
 
   const int warps = blockDim.x / kWarpSize;
@@ -147,22 +154,52 @@ __global__ void __launch_bounds__(512) norm_bulk_kernel(const NormArgs a) {
       const uint8_t* xs = st + rl * row_bytes;
       uint4 hv[V];
       float part[V];
+      if constexpr (kPacked) {
+        // vectors v and v + 1 summed side by side in packed fp32 pairs: each running sum keeps
+        // its own order and roundings (a vector past the row is zero and leaves its sum +0)
 #pragma unroll
-      for (int v = 0; v < V; ++v) {
-        const int c = sub + G * v;
-        part[v] = 0.0f;
-        if (c < nvec) {
-          uint4 raw = ld_shared_v4(xs + c * 16);
-          if constexpr (kAdd) {
-            raw = add_vec<E>(raw, ld_shared_v4(xs + a.rows_per_unit * row_bytes + c * 16));
-          }
-          hv[v] = raw;
-          float f[kVec];
-          unpack<E>(raw, f);
-#pragma unroll
-          for (int e = 0; e < kVec; ++e) part[v] = __fmaf_rn(f[e], f[e], part[v]);
-        } else {
+        for (int v = 0; v < V; ++v) {
+          const int c = sub + G * v;
           hv[v] = make_uint4(0, 0, 0, 0);
+          if (c < nvec) {
+            uint4 raw = ld_shared_v4(xs + c * 16);
+            if constexpr (kAdd) {
+              raw = add_vec<E>(raw, ld_shared_v4(xs + a.rows_per_unit * row_bytes + c * 16));
+            }
+            hv[v] = raw;
+          }
+        }
+#pragma unroll
+        for (int v = 0; v < V; v += 2) {
+          float f0[kVec], f1[kVec];
+          unpack<E>(hv[v], f0);
+          unpack<E>(hv[v + 1], f1);
+          uint64_t acc = f32x2(0.0f, 0.0f);
+#pragma unroll
+          for (int e = 0; e < kVec; ++e) {
+            const uint64_t p = f32x2(f0[e], f1[e]);
+            acc = f32x2_fma(p, p, acc);
+          }
+          f32x2_split(acc, part[v], part[v + 1]);
+        }
+      } else {
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          const int c = sub + G * v;
+          part[v] = 0.0f;
+          if (c < nvec) {
+            uint4 raw = ld_shared_v4(xs + c * 16);
+            if constexpr (kAdd) {
+              raw = add_vec<E>(raw, ld_shared_v4(xs + a.rows_per_unit * row_bytes + c * 16));
+            }
+            hv[v] = raw;
+            float f[kVec];
+            unpack<E>(raw, f);
+#pragma unroll
+            for (int e = 0; e < kVec; ++e) part[v] = __fmaf_rn(f[e], f[e], part[v]);
+          } else {
+            hv[v] = make_uint4(0, 0, 0, 0);
+          }
         }
       }
       float total;
@@ -194,8 +231,12 @@ __global__ void __launch_bounds__(512) norm_bulk_kernel(const NormArgs a) {
           const int c = sub + G * v;
           if (c < nvec) {
             if constexpr (kAdd) st_global_v4(res_row + c * kVec, hv[v]);
-            st_global_v4(out_row + c * kVec,
-                         normalize_vec<E>(hv[v], inv_rms, ld_shared_v4(wsm + c * 16)));
+            const uint4 wv = ld_shared_v4(wsm + c * 16);
+            if constexpr (kPacked) {
+              st_global_v4(out_row + c * kVec, normalize_vec_packed(hv[v], inv_rms, wv));
+            } else {
+              st_global_v4(out_row + c * kVec, normalize_vec<E>(hv[v], inv_rms, wv));
+            }
           }
         }
       }
