@@ -77,9 +77,10 @@ def test_module_attributes():
 
 
 # Up to 64 rows per SM (9472 on a B200) the row-block kernel runs; above, the bulk-copy kernels,
-# one per row width: both must equal the reference kernel bit for bit.
+# one per row width: both must equal the reference kernel bit for bit. 800 and 1600 leave the
+# last pair of a lane's vectors partly or wholly past the row (the paired sums of squares).
 BULK_SHAPES = [(10000, 1024), (12000, 128), (10000, 64), (10000, 768), (10000, 2048),
-               (10000, 4096), (10000, 96)]
+               (10000, 4096), (10000, 96), (10000, 800), (10000, 1600)]
 
 
 @pytest.mark.gpu
